@@ -1,0 +1,130 @@
+"""Generate golden fixtures by running the reference's own Python functions.
+
+Run in a container that has the reference checkout (read-only) at
+``$STREAMINDEX_REF`` (default ``/root/reference``)::
+
+    python tests/golden/make_golden.py
+
+The shipped reference drops the empty call parentheses of some method calls
+(``q.dim != 4``, ``qk.relu_``, ``(x).exp``, ``c_a.dim != 3``).  Rather than
+editing its source, the inputs are wrapped in a ``torch.Tensor`` subclass
+whose ``dim`` / ``relu_`` / ``exp`` attributes evaluate eagerly and return
+objects that are also callable (calling them returns themselves), so the
+reference's own lines run unchanged with their intended meaning.  Functions
+whose bodies were moved into dead branches are called with arguments that
+reach the live branch (``softmax_scale=None`` for ``reference_sparse_attn``;
+``n_compressed < top_k`` for ``build_csa_topk_idxs``).
+
+Outputs are written next to this script as ``*.pt``; the tests read only
+those files (the reference is never read at test time).
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+
+import torch
+
+REF = os.environ.get("STREAMINDEX_REF", "/root/reference")
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+class _CallableInt(int):
+    def __call__(self):
+        return int(self)
+
+
+class Fixed(torch.Tensor):
+    """Tensor whose dropped-parenthesis attributes behave as the calls they meant."""
+
+    def __call__(self):
+        return self
+
+    @property
+    def dim(self):  # type: ignore[override]
+        return _CallableInt(torch.Tensor.dim(self))
+
+    @property
+    def relu_(self):  # type: ignore[override]
+        torch.Tensor.relu_(self)
+        return self
+
+    @property
+    def exp(self):  # type: ignore[override]
+        return torch.Tensor.exp(self)
+
+    @property
+    def abs(self):  # type: ignore[override]
+        return torch.Tensor.abs(self)
+
+
+def fx(t: torch.Tensor) -> torch.Tensor:
+    return t.as_subclass(Fixed)
+
+
+def plain(t):
+    return t.as_subclass(torch.Tensor) if isinstance(t, torch.Tensor) else t
+
+
+def _load(name, path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def main():
+    sys.path.insert(0, REF)
+    from flash_sparse import reference as R  # noqa: E402
+    from flash_sparse import csa as C  # noqa: E402
+
+    parity = _load("ref_parity", os.path.join(REF, "eval", "test_v4_indexer_parity.py"))
+    sys.path.insert(0, os.path.dirname(HERE))
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle.inputs import indexer_inputs, attn_inputs  # noqa: E402
+
+    out = {}
+
+    # 1. lightning indexer + materialise-then-topk with post-mask (V4 dims, small S)
+    cases = [
+        ("idx_v4", dict(B=1, S=128, H=64, D=128, T=32), 16, 4, 0),
+        ("idx_unaligned", dict(B=1, S=47, H=16, D=32, T=73), 16, 1, 901),
+        ("idx_b2", dict(B=2, S=96, H=32, D=64, T=24), 8, 4, 7),
+    ]
+    for name, shp, top_k, ratio, seed in cases:
+        q, k, w = indexer_inputs(shp["B"], shp["S"], shp["H"], shp["D"], shp["T"], seed=seed)
+        scores = plain(R.reference_lightning_indexer(fx(q), fx(k), fx(w)))
+        idx = plain(parity._materialize_topk(fx(q), fx(k), fx(w), top_k, ratio))
+        out[name] = dict(q=q, k=k, w=w, top_k=top_k, ratio=ratio, scores=scores.float(), topk_idx=idx.long())
+
+    # 2. sparse attention with sink, MLA-style D=576 (value = first 512 dims) and D=128
+    for name, shp, seed in [
+        ("attn_576", dict(B=1, S=24, H=16, D=576, N=64, K=32), 3),
+        ("attn_128", dict(B=2, S=16, H=8, D=128, N=40, K=16), 4),
+    ]:
+        q, kv, sink, idx = attn_inputs(shp["B"], shp["S"], shp["H"], shp["D"], shp["N"], shp["K"], ratio=1, seed=seed)
+        # one all-masked query and a masked slot pattern as in the reference tests
+        idx[0, 0] = -1
+        idx[:, :, 3::4] = -1
+        o = plain(R.reference_sparse_attn(fx(q.float()), fx(kv.float()), fx(sink), fx(idx), softmax_scale=None))
+        out[name] = dict(q=q, kv=kv, sink=sink, idx=idx, o=o.float())
+
+    # 3. compressor (non-overlap, zero scores/bias == mean pool), window and CSA index build
+    g = torch.Generator("cpu").manual_seed(11)
+    x = torch.randn((2, 30, 16), generator=g)
+    comp = plain(R.reference_token_compressor(fx(x), fx(torch.zeros_like(x)), fx(torch.zeros(4, 16)), 4, overlap=False))
+    out["compress"] = dict(x=x, m=4, out=comp)
+    out["window"] = dict(B=2, S=20, n_win=6, idx=plain(R._build_sliding_window_idxs(2, 20, 6, "cpu")))
+    sc = torch.randn((1, 40, 10), generator=g)
+    built = plain(C.build_csa_topk_idxs(sc, 8, 16, seq_len=40, n_compressed=10, m=4, device="cpu"))
+    out["csa_idx"] = dict(scores=sc, n_win=8, top_k=16, m=4, idx=built)
+
+    for name, d in out.items():
+        torch.save(d, os.path.join(HERE, f"{name}.pt"))
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main()
