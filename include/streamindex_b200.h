@@ -1,0 +1,67 @@
+/* StreamIndex-B200 C ABI.
+ *
+ * Plain pointers, sizes and a cudaStream_t; no framework types.  Every call
+ * only enqueues work on `stream` (no host synchronisation) and returns 0 on
+ * success or -1 with a message available from si_last_error().
+ *
+ * Each entry point replaces one function of the reference's Python API
+ * (tsukimia-hoshi/StreamIndex); the replaced function is cited beside it.
+ * Tensors are contiguous, row-major, device-resident.
+ *
+ * Workspaces are caller-allocated device buffers; their first 256 bytes hold
+ * a device status word (0 = ok, non-zero = a bounded wait inside a kernel
+ * timed out), readable with si_read_status().
+ */
+#ifndef STREAMINDEX_B200_H
+#define STREAMINDEX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SI_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SI_API __attribute__((visibility("default")))
+#else
+#define SI_API
+#endif
+
+SI_API int si_abi_version(void);
+SI_API const char* si_last_error(void);
+/* Synchronises `stream` and copies the workspace's status word to *status_out. */
+SI_API int si_read_status(const void* ws, int* status_out, cudaStream_t stream);
+
+/* Workspace bytes for si_indexer_topk on the current device. */
+SI_API size_t si_indexer_topk_ws_bytes(int B, int S, int T, int H, int D, int top_k);
+
+/* Fused lightning-indexer score + streaming top-k.
+ * Replaces chunked_indexer_topk (flash_sparse/triton/chunked_indexer.py:47-160)
+ * and indexer_score_topk (flash_sparse/triton/indexer_score.py:182-205).
+ *   q        [B,S,H,D]  bf16 (fp16 if ab_fp16)     H in {16,32,64,128}, D % 8 == 0, D <= 128
+ *   k        [B,T,D]    same dtype as q
+ *   w        [B,S,H]    fp32, or bf16 if w_is_bf16
+ *   causal_ratio > 0: key t is legal for query s iff t < (s+1)/causal_ratio;
+ *   causal_mask (nullable, [B,S,T] bytes, nonzero = legal) used when causal_ratio <= 0;
+ *   neither: all keys legal.
+ *   out_idx    [B,S,top_k] int64, sorted by score desc then index asc; -1 pads
+ *   out_scores [B,S,top_k] fp32; -inf pads
+ * Results do not depend on any chunking: the selection is exact. */
+SI_API int si_indexer_topk(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
+                    int H, int D, int top_k, int causal_ratio, const uint8_t* causal_mask, int64_t* out_idx,
+                    float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream);
+
+/* Materialised indexer scores, no mask.
+ * Replaces indexer_score (flash_sparse/triton/indexer_score.py:123-179).
+ *   out [B,S,T] fp32.  ws: at least 256 bytes (status word). */
+SI_API int si_indexer_score(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
+                     int H, int D, float* out, void* ws, size_t ws_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,22 @@
+// Host-side helpers shared by the C-ABI entry points: thread-local error
+// string, TMA tensor-map encoding, device queries.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace si {
+
+constexpr size_t kStatusBytes = 256;  // status word at the head of every workspace
+
+int fail(const char* fmt, ...);                      // records the message, returns -1
+int fail_cuda(const char* what, cudaError_t e);      // records "<what>: <cuda error>", returns -1
+int device_sm_count();
+// 2-D row-major tensor of 16-bit elements [rows, cols] (cols contiguous), box
+// [box_rows, box_cols] with the 128-byte swizzle.  dtype: 0 bf16, 1 fp16.
+int make_tmap_2d_16b(CUtensorMap* map, const void* base, int cols, uint64_t rows, int box_cols, int box_rows,
+                     int dtype);
+cudaError_t launch_fill_pad(int64_t* idx, float* scores, long long n, cudaStream_t stream);
+
+}  // namespace si

@@ -1,0 +1,711 @@
+// Fused indexer score + streaming top-k kernel, row-sort kernel and launchers.
+// Design notes are in indexer_topk.cuh.
+#include <cstdio>
+#include <cuda_bf16.h>
+
+#include "indexer_topk.cuh"
+
+namespace si {
+
+// ------------------------------------------------------------------ scheduling
+// Query blocks are visited in decreasing causal work (the last block of a
+// batch has the most legal keys) and dealt to CTAs in a zig-zag, so a static
+// schedule is balanced without an atomic work counter.
+__device__ __forceinline__ void block_coords(const IndexerParams& p, int i, int& b, int& blk) {
+  const int r = i / p.B;
+  b = i - r * p.B;
+  blk = p.nblk_per_batch - 1 - r;
+}
+
+__device__ __forceinline__ int block_index(int round, int cta, int grid) {
+  return round * grid + ((round & 1) ? (grid - 1 - cta) : cta);
+}
+
+// Number of legal keys of query s (mode-dependent upper bound on t).
+__device__ __forceinline__ int key_limit(const IndexerParams& p, int s) {
+  if (s >= p.S) return 0;
+  if (p.ratio > 0) {
+    const long long l = ((long long)s + 1) / p.ratio;
+    return l < p.T ? (int)l : p.T;
+  }
+  return p.T;
+}
+
+__device__ __forceinline__ int block_key_tiles(const IndexerParams& p, int QC, int blk) {
+  const int s_last = min(p.S, (blk + 1) * QC) - 1;
+  return ceil_div(key_limit(p, s_last), kKeysPerTile);
+}
+
+// ------------------------------------------------------------------ warp radix select
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+  uint32_t lo = (uint32_t)v, hi = (uint32_t)(v >> 32);
+  lo = __shfl_xor_sync(0xffffffffu, lo, m);
+  hi = __shfl_xor_sync(0xffffffffu, hi, m);
+  return ((unsigned long long)hi << 32) | lo;
+}
+
+// One warp: keep the `ksel` largest of the n (> ksel) distinct keys in buf,
+// compacted to buf[0, ksel), and return the smallest kept key.  hist is a
+// 256-entry shared scratch owned by this warp.
+__device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, int ksel, uint32_t* hist) {
+  const uint32_t lane = lane_id();
+  unsigned long long a = ~0ull, o = 0ull;
+  for (int i = lane; i < n; i += 32) {
+    const unsigned long long k = buf[i];
+    a &= k;
+    o |= k;
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    a &= shfl_xor_u64(a, m);
+    o |= shfl_xor_u64(o, m);
+  }
+  const unsigned long long diff = a ^ o;  // nonzero: keys are distinct and n >= 2
+  const int hb = 63 - __clzll((long long)diff);
+  unsigned long long mask = (hb == 63) ? 0ull : ~((2ull << hb) - 1ull);
+  unsigned long long prefix = a & mask;
+  int need = ksel;
+  int shift = hb >= 7 ? hb - 7 : 0;
+  while (true) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const unsigned long long k = buf[i];
+      if ((k & mask) == prefix) atomicAdd(&hist[(uint32_t)(k >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    uint32_t c[8];
+    uint32_t local = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = hist[lane * 8 + j];
+      local += c[j];
+    }
+    // inclusive suffix sum over lanes (lane 31 holds the highest digits)
+    uint32_t suf = local;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const uint32_t v = __shfl_down_sync(0xffffffffu, suf, m);
+      if (lane + m < 32) suf += v;
+    }
+    const uint32_t above_lane = suf - local;  // count in higher lanes
+    // the crossing lane: above_lane < need <= suf
+    const bool mine = above_lane < (uint32_t)need && (uint32_t)need <= suf;
+    int digit = 0;
+    uint32_t above = above_lane, eq = 0;
+    if (mine) {
+#pragma unroll
+      for (int j = 7; j >= 0; --j) {
+        if (above + c[j] >= (uint32_t)need) {
+          digit = (int)lane * 8 + j;
+          eq = c[j];
+          break;
+        }
+        above += c[j];
+      }
+    }
+    const uint32_t who = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+    digit = __shfl_sync(0xffffffffu, digit, who);
+    above = __shfl_sync(0xffffffffu, above, who);
+    eq = __shfl_sync(0xffffffffu, eq, who);
+    need -= (int)above;
+    prefix |= (unsigned long long)digit << shift;
+    mask |= 0xFFull << shift;
+    __syncwarp();
+    if ((int)eq == need || shift == 0) break;
+    shift = shift >= 8 ? shift - 8 : 0;
+  }
+  // keys >= prefix are exactly the top ksel; compact in place (stable, never
+  // writes ahead of the chunk being read)
+  const unsigned long long theta = prefix;
+  int out = 0;
+  unsigned long long kmin = ~0ull;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + (int)lane;
+    const unsigned long long k = i < n ? buf[i] : 0ull;
+    const bool sel = i < n && k >= theta;
+    const uint32_t bal = __ballot_sync(0xffffffffu, sel);
+    if (sel) {
+      buf[out + __popc(bal & lt)] = k;
+      kmin = k < kmin ? k : kmin;
+    }
+    out += __popc(bal);
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const unsigned long long v = shfl_xor_u64(kmin, m);
+    kmin = v < kmin ? v : kmin;
+  }
+  __syncwarp();
+  return kmin;
+}
+
+}  // namespace si
+
+namespace si {
+
+struct __align__(8) IndexerSmemMisc {
+  uint64_t k_full[4], k_empty[4];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t q_full, q_empty;
+  unsigned long long thr[kMaxQC];
+  int cnt[kMaxQC];
+  int lim[kMaxQC];
+  uint32_t tmem_base;
+  int abort_flag;
+  float w[kQRows];
+  uint32_t hist[kEpiWarps][256];
+};
+
+__host__ __device__ inline int indexer_stages(int D) { return D <= 64 ? 4 : 2; }
+__host__ __device__ inline size_t indexer_smem_bytes(int D) {
+  const int na = D / 64;
+  return 1024 /*alignment slack*/ + (size_t)na * kQRows * 128 + (size_t)indexer_stages(D) * na * kKeysPerTile * 128 +
+         sizeof(IndexerSmemMisc);
+}
+
+// ------------------------------------------------------------------ epilogue
+// Warps 2..9.  Per (key tile, group): TMEM -> fp32 scores (ReLU, w, sum over
+// heads in-thread), release the accumulator, then feed the streaming top-k.
+template <int H, int MODE>
+__device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, IndexerSmemMisc* ms, uint32_t tmem,
+                                                 int warp, uint32_t lane, int nrounds, int nblocks, int grid) {
+  constexpr int QC = kQRows / H;
+  constexpr int QG = kGroupCols / H;
+  constexpr int NQH = (kGroupCols / 2) / H;
+  const int e = warp - 2;
+  const int qd = warp & 3;  // TMEM lane quadrant this warp may access
+  const int hf = e >> 2;    // column half of each group
+  const int etid = e * 32 + (int)lane;
+  const uint32_t lt = (1u << lane) - 1u;
+  volatile int* abort_flag = &ms->abort_flag;
+  volatile int* vcnt = ms->cnt;
+  volatile unsigned long long* vthr = ms->thr;
+  uint32_t* hist = ms->hist[e];
+  unsigned long long* cand_cta = p.cand + (size_t)blockIdx.x * QC * p.cap;
+  uint32_t aph[2] = {0, 0};
+
+  for (int r = 0; r < nrounds; ++r) {
+    const int i = block_index(r, blockIdx.x, grid);
+    if (i >= nblocks) continue;
+    int b, blk;
+    block_coords(p, i, b, blk);
+    const int s0 = blk * QC;
+    const int ntiles = (MODE == kModeTopk) ? block_key_tiles(p, QC, blk) : ceil_div(p.T, kKeysPerTile);
+
+    named_bar(3, 32 * kEpiWarps);  // the previous block is done with w / lim / thr / cnt
+    for (int x = etid; x < QC * H; x += 32 * kEpiWarps) {
+      const int s = s0 + x / H;
+      float wv = 0.f;
+      if (s < p.S) {
+        const size_t off = ((size_t)b * p.S + s) * H + (x % H);
+        wv = p.w_is_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.w)[off])
+                         : reinterpret_cast<const float*>(p.w)[off];
+      }
+      ms->w[x] = wv;
+    }
+    if (etid < QC) {
+      ms->lim[etid] = key_limit(p, s0 + etid);
+      ms->thr[etid] = 0ull;
+      ms->cnt[etid] = 0;
+    }
+    named_bar(3, 32 * kEpiWarps);
+
+    bool ok = true;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int tkey = t * kKeysPerTile + qd * 32 + (int)lane;
+      for (int g = 0; g < 2; ++g) {
+        if (!mbar_wait(&ms->acc_full[g], aph[g], abort_flag, p.status, kErrWaitAccFull)) {
+          ok = false;
+          break;
+        }
+        aph[g] ^= 1;
+        tc_fence_after();
+        float acc[NQH];
+#pragma unroll
+        for (int jj = 0; jj < NQH; ++jj) acc[jj] = 0.f;
+        const uint32_t tbase = tmem + ((uint32_t)(qd * 32) << 16) + g * kGroupCols + hf * (kGroupCols / 2);
+        const float* wrow = ms->w + g * kGroupCols + hf * (kGroupCols / 2);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v0[32], v1[32];
+          tmem_ld32x2_sync(tbase + c * 64, tbase + c * 64 + 32, v0, v1);
+#pragma unroll
+          for (int h4 = 0; h4 < 8; ++h4) {
+            const float4 wa = reinterpret_cast<const float4*>(wrow + c * 64)[h4];
+            const float4 wb = reinterpret_cast<const float4*>(wrow + c * 64 + 32)[h4];
+            const int ca = c * 64 + h4 * 4, cb = c * 64 + 32 + h4 * 4;
+            acc[ca / H] = fmaf(wa.x, fmaxf(v0[h4 * 4 + 0], 0.f), acc[ca / H]);
+            acc[ca / H] = fmaf(wa.y, fmaxf(v0[h4 * 4 + 1], 0.f), acc[ca / H]);
+            acc[ca / H] = fmaf(wa.z, fmaxf(v0[h4 * 4 + 2], 0.f), acc[ca / H]);
+            acc[ca / H] = fmaf(wa.w, fmaxf(v0[h4 * 4 + 3], 0.f), acc[ca / H]);
+            acc[cb / H] = fmaf(wb.x, fmaxf(v1[h4 * 4 + 0], 0.f), acc[cb / H]);
+            acc[cb / H] = fmaf(wb.y, fmaxf(v1[h4 * 4 + 1], 0.f), acc[cb / H]);
+            acc[cb / H] = fmaf(wb.z, fmaxf(v1[h4 * 4 + 2], 0.f), acc[cb / H]);
+            acc[cb / H] = fmaf(wb.w, fmaxf(v1[h4 * 4 + 3], 0.f), acc[cb / H]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ms->acc_empty[g]);
+
+        if (MODE == kModeScore) {
+#pragma unroll
+          for (int jj = 0; jj < NQH; ++jj) {
+            const int s = s0 + g * QG + hf * NQH + jj;
+            if (s < p.S && tkey < p.T) p.out_scores[((size_t)b * p.S + s) * p.T + tkey] = acc[jj];
+          }
+          continue;
+        }
+
+        // ---- streaming top-k: make room, then insert this tile's candidates
+        named_bar(1 + hf, 128);
+        bool any = false;
+#pragma unroll
+        for (int jj = 0; jj < NQH; ++jj) any |= vcnt[g * QG + hf * NQH + jj] > p.cap - kKeysPerTile;
+        if (any) {
+#pragma unroll
+          for (int jj = 0; jj < NQH; ++jj) {
+            const int j = g * QG + hf * NQH + jj;
+            if ((jj & 3) == qd && vcnt[j] > p.cap - kKeysPerTile) {
+              const unsigned long long th = warp_select_topk(cand_cta + (size_t)j * p.cap, vcnt[j], p.ksel, hist);
+              if (lane == 0) {
+                vthr[j] = th;
+                vcnt[j] = p.ksel;
+              }
+            }
+          }
+          named_bar(1 + hf, 128);
+        }
+#pragma unroll
+        for (int jj = 0; jj < NQH; ++jj) {
+          const int j = g * QG + hf * NQH + jj;
+          bool legal = tkey < ms->lim[j];
+          if (MODE == kModeTopkMask && legal)
+            legal = p.mask[((size_t)b * p.S + (s0 + j)) * p.T + tkey] != 0;
+          const unsigned long long key = make_key(acc[jj], tkey);
+          const bool pass = legal && key > vthr[j];
+          const uint32_t bal = __ballot_sync(0xffffffffu, pass);
+          if (bal) {
+            const int leader = __ffs(bal) - 1;
+            int base = 0;
+            if ((int)lane == leader) base = atomicAdd(&ms->cnt[j], __popc(bal));
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if (pass) cand_cta[(size_t)j * p.cap + base + __popc(bal & lt)] = key;
+          }
+        }
+      }
+    }
+    if (!ok) break;
+
+    if (MODE != kModeScore) {
+      // ---- final selection and (unsorted) key write-out for this block's queries
+      named_bar(1 + hf, 128);
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+#pragma unroll
+        for (int jj = 0; jj < NQH; ++jj) {
+          const int j = g * QG + hf * NQH + jj;
+          const int s = s0 + j;
+          if ((jj & 3) != qd || s >= p.S) continue;
+          unsigned long long* buf = cand_cta + (size_t)j * p.cap;
+          int n = vcnt[j];
+          if (n > p.ksel) {
+            warp_select_topk(buf, n, p.ksel, hist);
+            n = p.ksel;
+          }
+          unsigned long long* dst = p.out_keys + ((size_t)b * p.S + s) * p.ksel;
+          for (int x = (int)lane; x < p.ksel; x += 32) dst[x] = x < n ? buf[x] : 0ull;
+        }
+      }
+    }
+  }
+}
+
+template <int H, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    indexer_topk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        IndexerParams p, uint32_t idesc) {
+  constexpr int QC = kQRows / H;         // queries per block
+  constexpr int QG = kGroupCols / H;     // queries per group
+  constexpr int NQH = (kGroupCols / 2) / H;  // queries per half-group (per epilogue warp)
+  static_assert(NQH >= 1 && QC <= kMaxQC, "unsupported head count");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NA = p.D / 64;
+  const int NST = indexer_stages(p.D);
+  uint8_t* sQ = smem;                                    // [NA][512 rows][128 B]
+  uint8_t* sK = smem + (size_t)NA * kQRows * 128;        // [NST][NA][128 rows][128 B]
+  IndexerSmemMisc* ms = reinterpret_cast<IndexerSmemMisc*>(sK + (size_t)NST * NA * kKeysPerTile * 128);
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t lane = lane_id();
+  const int grid = gridDim.x;
+  const int nblocks = p.B * p.nblk_per_batch;
+  const int nrounds = ceil_div(nblocks, grid);
+  volatile int* abort_flag = &ms->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&ms->k_full[i], 1);
+      mbar_init(&ms->k_empty[i], 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&ms->acc_full[g], 1);
+      mbar_init(&ms->acc_empty[g], kEpiWarps);
+    }
+    mbar_init(&ms->q_full, 1);
+    mbar_init(&ms->q_empty, 1);
+    ms->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&map_q);
+    prefetch_tmap(&map_k);
+  }
+  if (warp == 1) {
+    tmem_alloc(&ms->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ms->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t st = 0, kph = 0, qph = 0;
+      const uint32_t qbytes = (uint32_t)NA * kQRows * 128;
+      const uint32_t kbytes = (uint32_t)NA * kKeysPerTile * 128;
+      for (int r = 0; r < nrounds; ++r) {
+        const int i = block_index(r, blockIdx.x, grid);
+        if (i >= nblocks) continue;
+        int b, blk;
+        block_coords(p, i, b, blk);
+        const int ntiles = (MODE == kModeTopk) ? block_key_tiles(p, QC, blk) : ceil_div(p.T, kKeysPerTile);
+        if (ntiles == 0) continue;
+        if (!mbar_wait(&ms->q_empty, qph ^ 1, abort_flag, p.status, kErrWaitQ)) break;
+        qph ^= 1;
+        mbar_expect_tx(&ms->q_full, qbytes);
+        const int qrow = (b * p.S + blk * QC) * H;
+        for (int a = 0; a < NA; ++a)
+          for (int hh = 0; hh < 2; ++hh)
+            tma_load_2d(sQ + (size_t)a * kQRows * 128 + hh * 256 * 128, &map_q, &ms->q_full, a * 64,
+                        qrow + hh * 256);
+        const int krow = b * p.T;
+        bool ok = true;
+        for (int t = 0; t < ntiles; ++t) {
+          if (!mbar_wait(&ms->k_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&ms->k_full[st], kbytes);
+          uint8_t* dst = sK + (size_t)st * NA * kKeysPerTile * 128;
+          for (int a = 0; a < NA; ++a)
+            tma_load_2d(dst + (size_t)a * kKeysPerTile * 128, &map_k, &ms->k_full[st], a * 64,
+                        krow + t * kKeysPerTile);
+          if (++st == (uint32_t)NST) {
+            st = 0;
+            kph ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      uint32_t st = 0, kph = 0, qph = 0;
+      uint32_t aph[2] = {0, 0};
+      for (int r = 0; r < nrounds; ++r) {
+        const int i = block_index(r, blockIdx.x, grid);
+        if (i >= nblocks) continue;
+        int b, blk;
+        block_coords(p, i, b, blk);
+        const int ntiles = (MODE == kModeTopk) ? block_key_tiles(p, QC, blk) : ceil_div(p.T, kKeysPerTile);
+        if (ntiles == 0) continue;
+        if (!mbar_wait(&ms->q_full, qph, abort_flag, p.status, kErrWaitQ)) break;
+        qph ^= 1;
+        tc_fence_after();
+        bool ok = true;
+        for (int t = 0; t < ntiles && ok; ++t) {
+          if (!mbar_wait(&ms->k_full[st], kph, abort_flag, p.status, kErrWaitTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t kbase = smem_u32(sK + (size_t)st * NA * kKeysPerTile * 128);
+          for (int g = 0; g < 2; ++g) {
+            if (!mbar_wait(&ms->acc_empty[g], aph[g] ^ 1, abort_flag, p.status, kErrWaitAccEmpty)) {
+              ok = false;
+              break;
+            }
+            aph[g] ^= 1;
+            tc_fence_after();
+            const uint32_t qbase = smem_u32(sQ) + g * kGroupCols * 128;
+            const uint32_t d_tmem = tmem + g * kGroupCols;
+            for (int a = 0; a < NA; ++a) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t adesc = umma_desc_sw128(kbase + a * kKeysPerTile * 128 + kk * 32);
+                const uint64_t bdesc = umma_desc_sw128(qbase + a * kQRows * 128 + kk * 32);
+                umma_f16(d_tmem, adesc, bdesc, idesc, (a | kk) != 0);
+              }
+            }
+            umma_commit(&ms->acc_full[g]);
+          }
+          umma_commit(&ms->k_empty[st]);
+          if (++st == (uint32_t)NST) {
+            st = 0;
+            kph ^= 1;
+          }
+        }
+        umma_commit(&ms->q_empty);
+        if (!ok) break;
+      }
+    }
+  } else {
+    indexer_epilogue<H, MODE>(p, ms, tmem, warp, lane, nrounds, nblocks, grid);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace si
+
+namespace si {
+
+// ------------------------------------------------------------------ row sort
+// One warp per row: read ksel 64-bit keys (0 = empty slot), bitonic-sort them
+// descending in registers (E keys per lane, element i = r*32 + lane), and
+// decode into idx (int64, -1 for empty) and score (fp32, -inf for empty)
+// in place of the keys.
+template <int E>
+__global__ void __launch_bounds__(256) topk_row_sort_kernel(unsigned long long* keys_io, float* scores_out,
+                                                            long long rows, int ksel) {
+  constexpr int P = E * 32;
+  const long long row = (long long)blockIdx.x * 8 + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  unsigned long long* kr = keys_io + row * ksel;
+  unsigned long long v[E];
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const int i = r * 32 + lane;
+    v[r] = i < ksel ? kr[i] : 0ull;
+  }
+#pragma unroll
+  for (int size = 2; size <= P; size <<= 1) {
+#pragma unroll
+    for (int j = size >> 1; j >= 1; j >>= 1) {
+      if (j >= 32) {
+        const int rj = j / 32;
+#pragma unroll
+        for (int r = 0; r < E; ++r) {
+          if ((r & rj) == 0) {
+            const int r2 = r | rj;
+            const bool desc = (((r * 32 + lane) & size) == 0);
+            const unsigned long long a = v[r], c = v[r2];
+            const bool sw = desc ? (a < c) : (a > c);
+            v[r] = sw ? c : a;
+            v[r2] = sw ? a : c;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < E; ++r) {
+          const unsigned long long o = shfl_xor_u64(v[r], j);
+          const int i = r * 32 + lane;
+          const bool desc = ((i & size) == 0);
+          const bool lower = (lane & j) == 0;
+          const bool take_max = (lower == desc);
+          v[r] = take_max ? (o > v[r] ? o : v[r]) : (o < v[r] ? o : v[r]);
+        }
+      }
+    }
+  }
+  long long* ir = reinterpret_cast<long long*>(kr);
+  float* sr = scores_out + row * ksel;
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const int i = r * 32 + lane;
+    if (i < ksel) {
+      const unsigned long long k = v[r];
+      ir[i] = k ? (long long)(0xFFFFFFFFu - (uint32_t)k) : -1ll;
+      sr[i] = k ? unord_f32((uint32_t)(k >> 32)) : -INFINITY;
+    }
+  }
+}
+
+}  // namespace si
+
+// ==================================================================== host side
+#include "capi_common.h"
+#include "../../include/streamindex_b200.h"
+
+namespace si {
+
+static int pick_cap(int ksel) { return ((2 * ksel + kKeysPerTile + 31) / 32) * 32; }
+
+static int indexer_grid(int nblocks) {
+  const int sms = device_sm_count();
+  return nblocks < sms ? nblocks : sms;
+}
+
+size_t indexer_ws_bytes(int B, int S, int H, int ksel) {
+  const int QC = kQRows / H;
+  const int nblocks = B * ceil_div(S, QC);
+  const int grid = indexer_grid(nblocks > 0 ? nblocks : 1);
+  return kStatusBytes + (size_t)grid * QC * pick_cap(ksel) * sizeof(unsigned long long);
+}
+
+template <int H, int MODE>
+static cudaError_t launch_indexer_t(const CUtensorMap& mq, const CUtensorMap& mk, const IndexerParams& p, int grid,
+                                    uint32_t idesc, cudaStream_t stream) {
+  const size_t smem = indexer_smem_bytes(p.D);
+  static bool configured = false;  // one-time attribute set, idempotent
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(indexer_topk_kernel<H, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)indexer_smem_bytes(128));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  indexer_topk_kernel<H, MODE><<<grid, kThreads, smem, stream>>>(mq, mk, p, idesc);
+  return cudaGetLastError();
+}
+
+template <int MODE>
+static cudaError_t launch_indexer_h(const CUtensorMap& mq, const CUtensorMap& mk, const IndexerParams& p, int grid,
+                                    uint32_t idesc, cudaStream_t stream) {
+  switch (p.H) {
+    case 16: return launch_indexer_t<16, MODE>(mq, mk, p, grid, idesc, stream);
+    case 32: return launch_indexer_t<32, MODE>(mq, mk, p, grid, idesc, stream);
+    case 64: return launch_indexer_t<64, MODE>(mq, mk, p, grid, idesc, stream);
+    case 128: return launch_indexer_t<128, MODE>(mq, mk, p, grid, idesc, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+static cudaError_t launch_row_sort(unsigned long long* keys, float* scores, long long rows, int ksel,
+                                   cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  int p = 32;
+  while (p < ksel) p <<= 1;
+  switch (p / 32) {
+    case 1: topk_row_sort_kernel<1><<<grid, 256, 0, stream>>>(keys, scores, rows, ksel); break;
+    case 2: topk_row_sort_kernel<2><<<grid, 256, 0, stream>>>(keys, scores, rows, ksel); break;
+    case 4: topk_row_sort_kernel<4><<<grid, 256, 0, stream>>>(keys, scores, rows, ksel); break;
+    case 8: topk_row_sort_kernel<8><<<grid, 256, 0, stream>>>(keys, scores, rows, ksel); break;
+    case 16: topk_row_sort_kernel<16><<<grid, 256, 0, stream>>>(keys, scores, rows, ksel); break;
+    case 32: topk_row_sort_kernel<32><<<grid, 256, 0, stream>>>(keys, scores, rows, ksel); break;
+    case 64: topk_row_sort_kernel<64><<<grid, 256, 0, stream>>>(keys, scores, rows, ksel); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// Shared argument checks for the indexer entry points.
+static int check_indexer_args(const void* q, const void* k, const void* w, int B, int S, int T, int H, int D) {
+  if (!q || !k || !w) return fail("indexer: null input pointer");
+  if (B < 1 || S < 0 || T < 0) return fail("indexer: bad B/S/T (B=%d S=%d T=%d)", B, S, T);
+  if (H != 16 && H != 32 && H != 64 && H != 128) return fail("indexer: H_I must be 16, 32, 64 or 128 (got %d)", H);
+  if (D < 8 || D > 128 || D % 8) return fail("indexer: D_I must be a multiple of 8 in [8,128] (got %d)", D);
+  if (((uintptr_t)q | (uintptr_t)k) & 15) return fail("indexer: q and k must be 16-byte aligned");
+  if ((long long)B * S * H + 1024 >= (1ll << 31) || (long long)B * T + 256 >= (1ll << 31))
+    return fail("indexer: B*S*H or B*T exceeds the 2^31 TMA coordinate range");
+  return 0;
+}
+
+static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
+                       int H, int D, int ksel, int ratio, const uint8_t* mask, int mode, int64_t* out_idx,
+                       float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (int rc = check_indexer_args(q, k, w, B, S, T, H, D)) return rc;
+  if (!ws) return fail("indexer: null workspace");
+  const size_t need = mode == kModeScore ? kStatusBytes : indexer_ws_bytes(B, S, H, ksel);
+  if (ws_bytes < need) return fail("indexer: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  int* status = reinterpret_cast<int*>(ws);
+  if (cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream)) return fail_cuda("indexer: status reset", e);
+  const long long rows = (long long)B * S;
+  if (rows == 0) return 0;
+  if (mode != kModeScore && T == 0) {
+    // no keys: every slot is padding
+    return launch_fill_pad(out_idx, out_scores, rows * ksel, stream);
+  }
+  if (mode == kModeScore && T == 0) return 0;
+
+  const int Dp = ((D + 63) / 64) * 64;
+  CUtensorMap mq, mk;
+  const int dt = ab_fp16 ? 1 : 0;
+  if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, 256, dt)) return rc;
+  if (int rc = make_tmap_2d_16b(&mk, k, D, (uint64_t)B * T, 64, kKeysPerTile, dt)) return rc;
+
+  IndexerParams p{};
+  p.B = B; p.S = S; p.T = T; p.H = H; p.D = Dp;
+  p.ratio = ratio > 0 ? ratio : 0;
+  p.ksel = ksel;
+  p.cap = pick_cap(ksel > 0 ? ksel : 1);
+  p.w_is_bf16 = w_is_bf16;
+  p.w = w;
+  p.mask = mask;
+  p.out_keys = reinterpret_cast<unsigned long long*>(out_idx);
+  p.out_scores = out_scores;
+  p.cand = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(ws) + kStatusBytes);
+  p.status = status;
+  const int QC = kQRows / H;
+  p.nblk_per_batch = ceil_div(S, QC);
+  const int grid = indexer_grid(B * p.nblk_per_batch);
+  const uint32_t idesc = umma_idesc_f16(kKeysPerTile, kGroupCols, ab_fp16 ? 0 : 1);
+  cudaError_t e;
+  if (mode == kModeTopk) e = launch_indexer_h<kModeTopk>(mq, mk, p, grid, idesc, stream);
+  else if (mode == kModeTopkMask) e = launch_indexer_h<kModeTopkMask>(mq, mk, p, grid, idesc, stream);
+  else e = launch_indexer_h<kModeScore>(mq, mk, p, grid, idesc, stream);
+  if (e != cudaSuccess) return fail_cuda("indexer: kernel launch", e);
+  if (mode != kModeScore) {
+    e = launch_row_sort(p.out_keys, out_scores, rows, ksel, stream);
+    if (e != cudaSuccess) return fail_cuda("indexer: row-sort launch", e);
+  }
+  return 0;
+}
+
+}  // namespace si
+
+extern "C" {
+
+size_t si_indexer_topk_ws_bytes(int B, int S, int T, int H, int D, int top_k) {
+  (void)T;
+  (void)D;
+  if (H != 16 && H != 32 && H != 64 && H != 128) H = 16;
+  if (B < 1) B = 1;
+  if (S < 1) S = 1;
+  return si::indexer_ws_bytes(B, S, H, top_k > 0 ? top_k : 1);
+}
+
+int si_indexer_topk(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
+                    int H, int D, int top_k, int causal_ratio, const uint8_t* causal_mask, int64_t* out_idx,
+                    float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (top_k < 1 || top_k > 2048) return si::fail("indexer_topk: top_k must be in [1, 2048] (got %d)", top_k);
+  if (!out_idx || !out_scores) return si::fail("indexer_topk: null output pointer");
+  const int mode = causal_ratio > 0 ? si::kModeTopk : (causal_mask ? si::kModeTopkMask : si::kModeTopk);
+  return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, top_k, causal_ratio > 0 ? causal_ratio : 0,
+                         causal_mask, mode, out_idx, out_scores, ws, ws_bytes, stream);
+}
+
+int si_indexer_score(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
+                     int H, int D, float* out, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (!out) return si::fail("indexer_score: null output pointer");
+  return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, 1, 0, nullptr, si::kModeScore, nullptr, out,
+                         ws, ws_bytes, stream);
+}
+
+}  // extern "C"

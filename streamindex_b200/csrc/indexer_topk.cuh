@@ -1,0 +1,81 @@
+// Fused lightning-indexer score + streaming top-k for sm_100a.
+//
+// Math (flash_sparse/reference.py:163-168, eq. 16 of the V4 report):
+//   I[b,s,t] = sum_h w[b,s,h] * relu(q[b,s,h,:] . k[b,t,:])
+// followed by the causal mask t < (s+1)//ratio (flash_sparse/triton/chunked_indexer.py:137)
+// and a per-query top-k in the order (score desc, index asc)
+// (docs/streaming_topk.md:48-66).  The [B,S,T] score tensor is never written
+// (except in the explicit materialise mode used by indexer_score).
+//
+// Mapping.  One persistent CTA per SM owns a "query block" of QC = 512/H
+// consecutive queries at a time.  Their Q rows ([QC*H, D] bf16, 128-byte
+// swizzled) stay resident in shared memory.  Keys stream through in tiles of
+// 128 rows (TMA), and the tensor core computes, per tile and per query group
+// g (two groups of 256 (query, head) columns):
+//     C_g[t, (s,h)] = k[t] . q[s,h]      M = 128 keys, N = 256, K = D
+// into TMEM columns [256g, 256g+256).  Keys on M means each epilogue thread
+// owns one key row, so ReLU, the fp32 w multiply and the sum over heads run
+// inside the thread with no cross-thread reduction.  The two groups form a
+// double buffer: the epilogue of group 0 overlaps the MMAs of group 1.
+//
+// Warp roles (320 threads):
+//   warp 0      TMA producer (Q block, K tiles)
+//   warp 1      TMEM allocator + single-thread UMMA issuer
+//   warps 2..9  epilogue: scores + streaming top-k.  Warp w reads TMEM lanes
+//               32*(w%4)..+32; warps 2-5 take columns [0,128) of each group,
+//               warps 6-9 columns [128,256).
+//
+// Streaming top-k.  Each query keeps, in a global workspace slab, a candidate
+// buffer of CAP 64-bit keys  key = ord(score) << 32 | (2^32-1 - t)  (larger
+// key = better under the reference's order).  A key enters the buffer iff it
+// beats the query's threshold key (the smallest key kept at the last flush,
+// 0 before).  When a buffer could overflow on the next tile, one warp runs an
+// exact radix select on it (8-bit digits over the 64-bit key), compacts it to
+// the top K and raises the threshold.  Selection is exact, so the result is
+// the exact top-K under the total order.  At the end of a query block the
+// kept keys are written unsorted into the idx output; a row-sort kernel turns
+// them into (idx int64, score fp32) sorted descending, padded with -1 / -inf.
+#pragma once
+#include "ptx.cuh"
+
+namespace si {
+
+constexpr int kKeysPerTile = 128;   // UMMA M
+constexpr int kGroupCols = 256;     // UMMA N per group
+constexpr int kQRows = 512;         // (query, head) rows resident per block
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kMaxQC = 32;          // H >= 16
+
+enum IndexerMode : int { kModeTopk = 0, kModeTopkMask = 1, kModeScore = 2 };
+
+struct IndexerParams {
+  int B, S, T, H, D;          // D is the padded head dim (multiple of 64, <= 128)
+  int ratio;                  // > 0: causal t < (s+1)//ratio ; 0: none
+  int ksel;                   // top-k width (selection size)
+  int cap;                    // candidate buffer capacity per query (multiple of 32, >= ksel + 128)
+  int w_is_bf16;
+  const void* w;              // [B,S,H] fp32 or bf16, contiguous
+  const uint8_t* mask;        // [B,S,T] bool (mode 1), contiguous
+  unsigned long long* out_keys;  // [B,S,ksel] (aliases the int64 idx output) — topk modes
+  float* out_scores;          // [B,S,T] — score mode
+  unsigned long long* cand;   // workspace: gridDim.x * QC * cap keys
+  int* status;                // device status word
+  int nblk_per_batch;         // ceil(S / QC)
+};
+
+__host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// Order-preserving map of an fp32 score to uint32 (larger float -> larger uint).
+__device__ __forceinline__ uint32_t ord_f32(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float unord_f32(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+__device__ __forceinline__ unsigned long long make_key(float score, int t) {
+  return ((unsigned long long)ord_f32(score) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)t);
+}
+
+}  // namespace si

@@ -1,0 +1,137 @@
+"""Lightning indexer + top-k on B200: the reference's Python API over the C ABI.
+
+* :func:`chunked_indexer_topk` — ``flash_sparse/triton/chunked_indexer.py:47-160``
+* :func:`indexer_score`        — ``flash_sparse/triton/indexer_score.py:123-179``
+* :func:`indexer_score_topk`   — ``flash_sparse/triton/indexer_score.py:182-205``
+
+Same argument names, meanings and error types as the reference: shape and
+device problems raise ``AssertionError`` (checked here, before the C call),
+unsupported head counts raise ``ValueError``, and a non-zero status from the
+library raises :class:`streamindex_b200._lib.SIError` (a ``RuntimeError``).
+There is no CPU fallback: inputs must be CUDA tensors.
+
+All three run one fused kernel (tcgen05 GEMM with the ReLU / head-weight /
+mask epilogue and an exact streaming top-k) plus a row sort; the
+``chunk_s`` / ``chunk_t`` hints of the reference are accepted and ignored,
+because the selection here is exact and keeps memory at O(S·k) regardless of
+chunking (the partition theorem of ``docs/streaming_topk.md:81-143`` is what
+made the reference's results chunk-independent too).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_HEADS = (16, 32, 64, 128)
+
+
+def _prep(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor):
+    assert q.is_cuda and k_idx.is_cuda and weights.is_cuda, "inputs must be CUDA tensors (no CPU fallback)"
+    assert q.dim() == 4 and k_idx.dim() == 3 and weights.dim() == 3
+    B, S, H, D = q.shape
+    B2, T, D2 = k_idx.shape
+    assert B2 == B and D2 == D, f"q/k shape mismatch: q={tuple(q.shape)}, k={tuple(k_idx.shape)}"
+    assert weights.shape == (B, S, H)
+    assert q.dtype in (torch.bfloat16, torch.float16), f"q must be bf16 or fp16, got {q.dtype}"
+    assert k_idx.dtype == q.dtype, "k_idx must have q's dtype"
+    if H not in _HEADS:
+        raise ValueError(f"H_I ({H}) must be one of {_HEADS}")
+    if D % 8 != 0 or D > 128:
+        raise ValueError(f"D_I ({D}) must be a multiple of 8 and at most 128")
+    q = q.contiguous()
+    k_idx = k_idx.contiguous()
+    if weights.dtype not in (torch.float32, torch.bfloat16):
+        weights = weights.float()
+    weights = weights.contiguous()
+    return q, k_idx, weights, (B, S, H, D, T)
+
+
+def _topk(q, k_idx, weights, top_k: int, width: int, ratio: Optional[int], mask: Optional[torch.Tensor]):
+    q, k_idx, weights, (B, S, H, D, T) = _prep(q, k_idx, weights)
+    dev = q.device
+    out_idx = torch.empty((B, S, width), dtype=torch.int64, device=dev)
+    out_scores = torch.empty((B, S, width), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws_bytes = lib.si_indexer_topk_ws_bytes(B, S, T, H, D, width)
+    with torch.cuda.device(dev):
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        m = None
+        if mask is not None:
+            m = mask.to(device=dev, dtype=torch.bool).expand(B, S, T).contiguous().view(torch.uint8)
+        _lib.check(lib.si_indexer_topk(
+            q.data_ptr(), k_idx.data_ptr(), weights.data_ptr(), int(weights.dtype == torch.bfloat16),
+            int(q.dtype == torch.float16), B, S, T, H, D, width, int(ratio or 0), _lib.ptr(m),
+            out_idx.data_ptr(), out_scores.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_handle(dev)))
+        _lib.maybe_check_status(ws, dev, "indexer_topk")
+    return out_idx, out_scores
+
+
+def chunked_indexer_topk(
+    q: torch.Tensor,
+    k_idx: torch.Tensor,
+    weights: torch.Tensor,
+    top_k: int,
+    *,
+    causal_mask: Optional[torch.Tensor] = None,
+    causal_ratio: Optional[int] = None,
+    chunk_s: int = 4096,
+    chunk_t: int = 4096,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Indexer + top-k.  Returns ``(idx int64 [B,S,top_k], scores fp32 [B,S,top_k])``.
+
+    Sorted by score descending, ties toward the smaller key index; slots with
+    no legal key are ``-1`` / ``-inf``.  ``causal_ratio=m`` applies
+    ``t < (s+1)//m`` on the fly; ``causal_mask`` ([B,S,T] bool, True = legal)
+    is the materialised alternative; they are mutually exclusive.
+    """
+    B, S = q.shape[0], q.shape[1]
+    T = k_idx.shape[1]
+    if causal_mask is not None:
+        assert causal_mask.shape == (B, S, T)
+        assert causal_ratio is None, "specify either causal_mask or causal_ratio, not both"
+    if causal_ratio is not None:
+        assert int(causal_ratio) >= 1, "causal_ratio must be a positive integer"
+    assert int(top_k) >= 1
+    del chunk_s, chunk_t  # tiling hints only; the result is chunk-independent
+    return _topk(q, k_idx, weights, int(top_k), int(top_k), causal_ratio, causal_mask)
+
+
+def indexer_score_topk(
+    q: torch.Tensor,
+    k_idx: torch.Tensor,
+    weights: torch.Tensor,
+    top_k: int,
+    *,
+    causal_mask: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Indexer + top-k of width ``min(top_k, T)``; ``-1`` / ``-inf`` where no legal key remains."""
+    B, S = q.shape[0], q.shape[1]
+    T = k_idx.shape[1]
+    if causal_mask is not None:
+        assert causal_mask.shape == (B, S, T)
+    width = min(int(top_k), T)
+    if width == 0:
+        dev = q.device
+        return (torch.empty((B, S, 0), dtype=torch.int64, device=dev),
+                torch.empty((B, S, 0), dtype=torch.float32, device=dev))
+    return _topk(q, k_idx, weights, width, width, None, causal_mask)
+
+
+def indexer_score(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    """Materialised lightning-indexer scores ``[B,S,T]`` fp32 (eq. 16), no mask."""
+    q, k_idx, weights, (B, S, H, D, T) = _prep(q, k_idx, weights)
+    dev = q.device
+    out = torch.empty((B, S, T), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(256, dtype=torch.uint8, device=dev)
+        _lib.check(lib.si_indexer_score(
+            q.data_ptr(), k_idx.data_ptr(), weights.data_ptr(), int(weights.dtype == torch.bfloat16),
+            int(q.dtype == torch.float16), B, S, T, H, D, out.data_ptr(), ws.data_ptr(), 256,
+            _lib.stream_handle(dev)))
+        _lib.maybe_check_status(ws, dev, "indexer_score")
+    return out
