@@ -146,7 +146,7 @@ __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, i
 
 namespace si {
 
-struct __align__(8) IndexerSmemMisc {
+struct __align__(16) IndexerSmemMisc {
   uint64_t k_full[4], k_empty[4];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_full, q_empty;
@@ -155,7 +155,7 @@ struct __align__(8) IndexerSmemMisc {
   int lim[kMaxQC];
   uint32_t tmem_base;
   int abort_flag;
-  float w[kQRows];
+  alignas(16) float w[kQRows];
   uint32_t hist[kEpiWarps][256];
 };
 
