@@ -55,6 +55,24 @@ SI_API int si_indexer_topk(const void* q, const void* k, const void* w, int w_is
                     int H, int D, int top_k, int causal_ratio, const uint8_t* causal_mask, int64_t* out_idx,
                     float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+/* si_indexer_topk with two extensions used by S-sharding and profiling.
+ *   s_offset: global position of local query 0; the causal limit of local
+ *             query s is (s_offset + s + 1) / causal_ratio.  q, w and the
+ *             outputs cover only the local queries.
+ *   flags:    SI_FLAG_SKIP_SORT leaves out_idx holding the unsorted 64-bit
+ *             selection keys (score order-key << 32 | 0xFFFFFFFF - index,
+ *             0 = empty) for a later si_topk_row_sort; out_scores untouched. */
+#define SI_FLAG_SKIP_SORT 1u
+SI_API int si_indexer_topk_ex(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S,
+                              int T, int H, int D, int top_k, int causal_ratio, const uint8_t* causal_mask,
+                              long long s_offset, unsigned flags, int64_t* out_idx, float* out_scores, void* ws,
+                              size_t ws_bytes, cudaStream_t stream);
+
+/* Sorts `rows` rows of top_k selection keys (as left by SI_FLAG_SKIP_SORT)
+ * descending and decodes them in place into int64 indices (-1 pads) and
+ * fp32 scores (-inf pads). */
+SI_API int si_topk_row_sort(int64_t* idx_keys, float* out_scores, long long rows, int top_k, cudaStream_t stream);
+
 /* Materialised indexer scores, no mask.
  * Replaces indexer_score (flash_sparse/triton/indexer_score.py:123-179).
  *   out [B,S,T] fp32.  ws: at least 256 bytes (status word). */

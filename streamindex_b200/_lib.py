@@ -25,6 +25,10 @@ SIGNATURES = {
     "si_indexer_topk_ws_bytes": (c_size_t, [c_int] * 6),
     "si_indexer_topk": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                 c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "si_indexer_topk_ex": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                   c_int, c_int, c_void_p, ctypes.c_longlong, ctypes.c_uint, c_void_p, c_void_p,
+                                   c_void_p, c_size_t, c_void_p]),
+    "si_topk_row_sort": (c_int, [c_void_p, c_void_p, ctypes.c_longlong, c_int, c_void_p]),
     "si_indexer_score": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_size_t, c_void_p]),
 }

@@ -25,7 +25,7 @@ __device__ __forceinline__ int block_index(int round, int cta, int grid) {
 __device__ __forceinline__ int key_limit(const IndexerParams& p, int s) {
   if (s >= p.S) return 0;
   if (p.ratio > 0) {
-    const long long l = ((long long)s + 1) / p.ratio;
+    const long long l = ((long long)s + p.s_offset + 1) / p.ratio;
     return l < p.T ? (int)l : p.T;
   }
   return p.T;
@@ -629,8 +629,10 @@ static int check_indexer_args(const void* q, const void* k, const void* w, int B
 
 static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
                        int H, int D, int ksel, int ratio, const uint8_t* mask, int mode, int64_t* out_idx,
-                       float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                       float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream, long long s_offset = 0,
+                       unsigned flags = 0) {
   if (int rc = check_indexer_args(q, k, w, B, S, T, H, D)) return rc;
+  if (s_offset < 0) return fail("indexer: negative s_offset");
   if (!ws) return fail("indexer: null workspace");
   const size_t need = mode == kModeScore ? kStatusBytes : indexer_ws_bytes(B, S, H, ksel);
   if (ws_bytes < need) return fail("indexer: workspace too small (%zu < %zu bytes)", ws_bytes, need);
@@ -664,6 +666,7 @@ static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf1
   p.status = status;
   const int QC = kQRows / H;
   p.nblk_per_batch = ceil_div(S, QC);
+  p.s_offset = s_offset;
   const int grid = indexer_grid(B * p.nblk_per_batch);
   const uint32_t idesc = umma_idesc_f16(kKeysPerTile, kGroupCols, ab_fp16 ? 0 : 1);
   cudaError_t e;
@@ -671,7 +674,7 @@ static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf1
   else if (mode == kModeTopkMask) e = launch_indexer_h<kModeTopkMask>(mq, mk, p, grid, idesc, stream);
   else e = launch_indexer_h<kModeScore>(mq, mk, p, grid, idesc, stream);
   if (e != cudaSuccess) return fail_cuda("indexer: kernel launch", e);
-  if (mode != kModeScore) {
+  if (mode != kModeScore && !(flags & SI_FLAG_SKIP_SORT)) {
     e = launch_row_sort(p.out_keys, out_scores, rows, ksel, stream);
     if (e != cudaSuccess) return fail_cuda("indexer: row-sort launch", e);
   }
@@ -699,6 +702,24 @@ int si_indexer_topk(const void* q, const void* k, const void* w, int w_is_bf16, 
   const int mode = causal_ratio > 0 ? si::kModeTopk : (causal_mask ? si::kModeTopkMask : si::kModeTopk);
   return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, top_k, causal_ratio > 0 ? causal_ratio : 0,
                          causal_mask, mode, out_idx, out_scores, ws, ws_bytes, stream);
+}
+
+int si_indexer_topk_ex(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
+                       int H, int D, int top_k, int causal_ratio, const uint8_t* causal_mask, long long s_offset,
+                       unsigned flags, int64_t* out_idx, float* out_scores, void* ws, size_t ws_bytes,
+                       cudaStream_t stream) {
+  if (top_k < 1 || top_k > 2048) return si::fail("indexer_topk: top_k must be in [1, 2048] (got %d)", top_k);
+  if (!out_idx || !out_scores) return si::fail("indexer_topk: null output pointer");
+  const int mode = causal_ratio > 0 ? si::kModeTopk : (causal_mask ? si::kModeTopkMask : si::kModeTopk);
+  return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, top_k, causal_ratio > 0 ? causal_ratio : 0,
+                         causal_mask, mode, out_idx, out_scores, ws, ws_bytes, stream, s_offset, flags);
+}
+
+int si_topk_row_sort(int64_t* idx_keys, float* out_scores, long long rows, int top_k, cudaStream_t stream) {
+  if (top_k < 1 || top_k > 2048) return si::fail("topk_row_sort: top_k must be in [1, 2048] (got %d)", top_k);
+  if (rows < 0 || (rows > 0 && (!idx_keys || !out_scores))) return si::fail("topk_row_sort: bad arguments");
+  cudaError_t e = si::launch_row_sort(reinterpret_cast<unsigned long long*>(idx_keys), out_scores, rows, top_k, stream);
+  return e == cudaSuccess ? 0 : si::fail_cuda("topk_row_sort: launch", e);
 }
 
 int si_indexer_score(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,

@@ -62,6 +62,7 @@ struct IndexerParams {
   unsigned long long* cand;   // workspace: gridDim.x * QC * cap keys
   int* status;                // device status word
   int nblk_per_batch;         // ceil(S / QC)
+  long long s_offset;         // global position of local query 0 (causal mask uses s_offset + s)
 };
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }

@@ -1,0 +1,79 @@
+"""Query-dimension (S) sharding of the indexer + top-k across GPUs.
+
+Each rank owns a contiguous query slice ``[s_lo, s_hi)`` of q / weights and a
+full replica of the compressed keys; queries are independent
+(``docs/streaming_topk.md:37-44`` of the reference), so the only exchanges
+are a broadcast of the keys from rank 0 and a gather of the per-slice
+results to rank 0 (NCCL over NVLink, via ``torch.distributed``).
+
+Causal work grows linearly with s (query s has ``min(T, (s+1)//ratio)``
+legal keys), so equal-length slices are unbalanced; ``balanced_bounds``
+places the boundaries at equal shares of the cumulative legal-pair count.
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def legal_pairs(S: int, T: int, ratio: Optional[int], lo: int = 0, hi: Optional[int] = None) -> int:
+    """Sum over s in [lo, hi) of min(T, (s+1)//ratio) (T per query without a ratio)."""
+    hi = S if hi is None else hi
+    if hi <= lo:
+        return 0
+    if not ratio:
+        return (hi - lo) * T
+    s = np.arange(lo, hi, dtype=np.int64)
+    return int(np.minimum(T, (s + 1) // int(ratio)).sum())
+
+
+def balanced_bounds(S: int, N: int, T: int, ratio: Optional[int], align: int = 128) -> List[int]:
+    """N+1 boundaries, multiples of ``align`` (except S), splitting the legal pairs evenly."""
+    if N <= 1:
+        return [0, S]
+    s = np.arange(S, dtype=np.int64)
+    w = np.minimum(T, (s + 1) // int(ratio)) if ratio else np.full(S, T, dtype=np.int64)
+    w = np.maximum(w, 1)  # every query costs at least its output write
+    cum = np.cumsum(w)
+    total = int(cum[-1])
+    bounds = [0]
+    for r in range(1, N):
+        b = int(np.searchsorted(cum, total * r / N))
+        b = min(S, max(bounds[-1], (b // align) * align))
+        bounds.append(b)
+    bounds.append(S)
+    return bounds
+
+
+def broadcast_keys(k_idx: torch.Tensor, src: int = 0) -> torch.Tensor:
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.broadcast(k_idx, src=src)
+    return k_idx
+
+
+def gather_to_rank0(local: torch.Tensor, bounds: List[int], full: Optional[torch.Tensor], dim: int = 1):
+    """Point-to-point gather of each rank's S-slice into ``full`` on rank 0."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        if full is not None and full.data_ptr() != local.data_ptr():
+            full.copy_(local)
+        return full
+    rank, world = dist.get_rank(), dist.get_world_size()
+    ops = []
+    if rank == 0:
+        assert full is not None
+        full.narrow(dim, bounds[0], bounds[1] - bounds[0]).copy_(local)
+        for r in range(1, world):
+            n = bounds[r + 1] - bounds[r]
+            if n > 0:
+                ops.append(dist.P2POp(dist.irecv, full.narrow(dim, bounds[r], n), r))
+    else:
+        if local.numel() > 0:
+            ops.append(dist.P2POp(dist.isend, local.contiguous(), 0))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    return full

@@ -135,3 +135,48 @@ def indexer_score(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor) -
             _lib.stream_handle(dev)))
         _lib.maybe_check_status(ws, dev, "indexer_score")
     return out
+
+
+class IndexerTopk:
+    """Pre-planned indexer + top-k for repeated calls on fixed shapes.
+
+    Holds the workspace and output buffers so a step enqueues exactly the
+    fused kernel and the row sort (plus a 4-byte status reset).  ``s_offset``
+    is the global position of local query 0, used when the query dimension is
+    sharded across ranks.  ``run(..., sort=False)`` leaves the selection keys
+    unsorted in ``out_idx`` so the two kernels can be timed separately;
+    ``sort()`` then finishes the step.
+    """
+
+    def __init__(self, B, S, T, H, D, top_k, causal_ratio=None, s_offset=0, device="cuda",
+                 q_dtype=torch.bfloat16, w_dtype=torch.float32):
+        if H not in _HEADS:
+            raise ValueError(f"H_I ({H}) must be one of {_HEADS}")
+        self.B, self.S, self.T, self.H, self.D, self.k = B, S, T, H, D, int(top_k)
+        self.ratio = int(causal_ratio or 0)
+        self.s_offset = int(s_offset)
+        self.device = torch.device(device)
+        self.fp16 = int(q_dtype == torch.float16)
+        self.w_bf16 = int(w_dtype == torch.bfloat16)
+        self.lib = _lib.load()
+        self.ws_bytes = self.lib.si_indexer_topk_ws_bytes(B, max(S, 1), T, H, D, self.k)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=self.device)
+        self.out_idx = torch.empty((B, S, self.k), dtype=torch.int64, device=self.device)
+        self.out_scores = torch.empty((B, S, self.k), dtype=torch.float32, device=self.device)
+
+    def run(self, q, k_idx, weights, sort: bool = True):
+        assert q.is_cuda and q.is_contiguous() and k_idx.is_contiguous() and weights.is_contiguous()
+        assert q.shape == (self.B, self.S, self.H, self.D) and k_idx.shape == (self.B, self.T, self.D)
+        _lib.check(self.lib.si_indexer_topk_ex(
+            q.data_ptr(), k_idx.data_ptr(), weights.data_ptr(), self.w_bf16, self.fp16, self.B, self.S, self.T,
+            self.H, self.D, self.k, self.ratio, None, self.s_offset, 0 if sort else 1, self.out_idx.data_ptr(),
+            self.out_scores.data_ptr(), self.ws.data_ptr(), self.ws_bytes, _lib.stream_handle(self.device)))
+        return self.out_idx, self.out_scores
+
+    def sort(self):
+        _lib.check(self.lib.si_topk_row_sort(self.out_idx.data_ptr(), self.out_scores.data_ptr(),
+                                             self.B * self.S, self.k, _lib.stream_handle(self.device)))
+        return self.out_idx, self.out_scores
+
+    def status(self) -> int:
+        return _lib.read_status(self.ws, self.device)
