@@ -44,17 +44,39 @@ __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v,
   return ((unsigned long long)hi << 32) | lo;
 }
 
+// Loads of the candidate buffer are issued kSelBatch at a time per lane
+// (independent loads, one latency per batch) — the buffer lives in global
+// memory (L1/L2 resident) and a dependent load per iteration would make every
+// pass latency-bound.
+constexpr int kSelBatch = 8;
+
+template <typename F>
+__device__ __forceinline__ void for_each_key(const unsigned long long* buf, int n, uint32_t lane, F&& f) {
+  for (int base = 0; base < n; base += 32 * kSelBatch) {
+    unsigned long long k[kSelBatch];
+#pragma unroll
+    for (int u = 0; u < kSelBatch; ++u) {
+      const int i = base + u * 32 + (int)lane;
+      k[u] = i < n ? buf[i] : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < kSelBatch; ++u) {
+      const int i = base + u * 32 + (int)lane;
+      if (i < n) f(k[u]);
+    }
+  }
+}
+
 // One warp: keep the `ksel` largest of the n (> ksel) distinct keys in buf,
 // compacted to buf[0, ksel), and return the smallest kept key.  hist is a
 // 256-entry shared scratch owned by this warp.
 __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, int ksel, uint32_t* hist) {
   const uint32_t lane = lane_id();
   unsigned long long a = ~0ull, o = 0ull;
-  for (int i = lane; i < n; i += 32) {
-    const unsigned long long k = buf[i];
+  for_each_key(buf, n, lane, [&](unsigned long long k) {
     a &= k;
     o |= k;
-  }
+  });
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) {
     a &= shfl_xor_u64(a, m);
@@ -70,10 +92,9 @@ __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, i
 #pragma unroll
     for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
     __syncwarp();
-    for (int i = lane; i < n; i += 32) {
-      const unsigned long long k = buf[i];
+    for_each_key(buf, n, lane, [&](unsigned long long k) {
       if ((k & mask) == prefix) atomicAdd(&hist[(uint32_t)(k >> shift) & 255u], 1u);
-    }
+    });
     __syncwarp();
     uint32_t c[8];
     uint32_t local = 0;
@@ -116,22 +137,31 @@ __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, i
     if ((int)eq == need || shift == 0) break;
     shift = shift >= 8 ? shift - 8 : 0;
   }
-  // keys >= prefix are exactly the top ksel; compact in place (stable, never
-  // writes ahead of the chunk being read)
+  // keys >= prefix are exactly the top ksel; compact in place (never writes
+  // ahead of the batch being read: all loads of a batch precede its stores)
   const unsigned long long theta = prefix;
   int out = 0;
   unsigned long long kmin = ~0ull;
   const uint32_t lt = (1u << lane) - 1u;
-  for (int base = 0; base < n; base += 32) {
-    const int i = base + (int)lane;
-    const unsigned long long k = i < n ? buf[i] : 0ull;
-    const bool sel = i < n && k >= theta;
-    const uint32_t bal = __ballot_sync(0xffffffffu, sel);
-    if (sel) {
-      buf[out + __popc(bal & lt)] = k;
-      kmin = k < kmin ? k : kmin;
+  for (int base = 0; base < n; base += 32 * kSelBatch) {
+    unsigned long long k[kSelBatch];
+#pragma unroll
+    for (int u = 0; u < kSelBatch; ++u) {
+      const int i = base + u * 32 + (int)lane;
+      k[u] = i < n ? buf[i] : 0ull;
     }
-    out += __popc(bal);
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < kSelBatch; ++u) {
+      const int i = base + u * 32 + (int)lane;
+      const bool sel = i < n && k[u] >= theta;
+      const uint32_t bal = __ballot_sync(0xffffffffu, sel);
+      if (sel) {
+        buf[out + __popc(bal & lt)] = k[u];
+        kmin = k[u] < kmin ? k[u] : kmin;
+      }
+      out += __popc(bal);
+    }
   }
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) {
@@ -164,6 +194,21 @@ __host__ __device__ inline size_t indexer_smem_bytes(int D) {
   const int na = D / 64;
   return 1024 /*alignment slack*/ + (size_t)na * kQRows * 128 + (size_t)indexer_stages(D) * na * kKeysPerTile * 128 +
          sizeof(IndexerSmemMisc);
+}
+
+// Packed fp32 helpers (sm_100 fma.rn.f32x2 on a 64-bit register pair).
+__device__ __forceinline__ unsigned long long relu2(float x, float y) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(fmaxf(x, 0.f)), "f"(fmaxf(y, 0.f)));
+  return r;
+}
+__device__ __forceinline__ void ffma2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float sum2(unsigned long long v) {
+  float x, y;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
+  return x + y;
 }
 
 // ------------------------------------------------------------------ epilogue
@@ -223,9 +268,12 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
         }
         aph[g] ^= 1;
         tc_fence_after();
-        float acc[NQH];
+        // acc2[jj] holds two partial sums (even / odd heads) updated with the
+        // packed fp32 FMA (fma.rn.f32x2): ReLU is one fmax per element, the
+        // weight multiply-add half an instruction per element.
+        unsigned long long acc2[NQH];
 #pragma unroll
-        for (int jj = 0; jj < NQH; ++jj) acc[jj] = 0.f;
+        for (int jj = 0; jj < NQH; ++jj) acc2[jj] = 0ull;
         const uint32_t tbase = tmem + ((uint32_t)(qd * 32) << 16) + g * kGroupCols + hf * (kGroupCols / 2);
         const float* wrow = ms->w + g * kGroupCols + hf * (kGroupCols / 2);
 #pragma unroll
@@ -233,20 +281,17 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
           float v0[32], v1[32];
           tmem_ld32x2_sync(tbase + c * 64, tbase + c * 64 + 32, v0, v1);
 #pragma unroll
-          for (int h4 = 0; h4 < 8; ++h4) {
-            const float4 wa = reinterpret_cast<const float4*>(wrow + c * 64)[h4];
-            const float4 wb = reinterpret_cast<const float4*>(wrow + c * 64 + 32)[h4];
-            const int ca = c * 64 + h4 * 4, cb = c * 64 + 32 + h4 * 4;
-            acc[ca / H] = fmaf(wa.x, fmaxf(v0[h4 * 4 + 0], 0.f), acc[ca / H]);
-            acc[ca / H] = fmaf(wa.y, fmaxf(v0[h4 * 4 + 1], 0.f), acc[ca / H]);
-            acc[ca / H] = fmaf(wa.z, fmaxf(v0[h4 * 4 + 2], 0.f), acc[ca / H]);
-            acc[ca / H] = fmaf(wa.w, fmaxf(v0[h4 * 4 + 3], 0.f), acc[ca / H]);
-            acc[cb / H] = fmaf(wb.x, fmaxf(v1[h4 * 4 + 0], 0.f), acc[cb / H]);
-            acc[cb / H] = fmaf(wb.y, fmaxf(v1[h4 * 4 + 1], 0.f), acc[cb / H]);
-            acc[cb / H] = fmaf(wb.z, fmaxf(v1[h4 * 4 + 2], 0.f), acc[cb / H]);
-            acc[cb / H] = fmaf(wb.w, fmaxf(v1[h4 * 4 + 3], 0.f), acc[cb / H]);
+          for (int h2 = 0; h2 < 16; ++h2) {
+            const int ca = c * 64 + h2 * 2, cb = c * 64 + 32 + h2 * 2;
+            const unsigned long long wa = reinterpret_cast<const unsigned long long*>(wrow + c * 64)[h2];
+            const unsigned long long wb = reinterpret_cast<const unsigned long long*>(wrow + c * 64 + 32)[h2];
+            ffma2(acc2[ca / H], relu2(v0[h2 * 2], v0[h2 * 2 + 1]), wa);
+            ffma2(acc2[cb / H], relu2(v1[h2 * 2], v1[h2 * 2 + 1]), wb);
           }
         }
+        float acc[NQH];
+#pragma unroll
+        for (int jj = 0; jj < NQH; ++jj) acc[jj] = sum2(acc2[jj]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ms->acc_empty[g]);
