@@ -73,6 +73,28 @@ SI_API int si_indexer_topk_ex(const void* q, const void* k, const void* w, int w
  * fp32 scores (-inf pads). */
 SI_API int si_topk_row_sort(int64_t* idx_keys, float* out_scores, long long rows, int top_k, cudaStream_t stream);
 
+/* Allocation-free si_indexer_topk.  No counterpart in the reference.
+ * For callers that cannot allocate device memory (a host runtime that owns
+ * the allocator and forbids plugins from calling cudaMalloc, or a caller that
+ * must not allocate while other work is in flight): the workspace is a
+ * file-scope device array of si_indexer_topk_noalloc_max_ws_bytes() bytes
+ * (16 MiB) held by every GPU that loads the library until process exit.
+ * Same arguments and results as si_indexer_topk without ws / ws_bytes.
+ *   - Rejects shapes whose workspace exceeds the maximum (-1, message in
+ *     si_last_error()); si_indexer_topk_ws_bytes() tells the need.
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (other
+ *     streams, other host threads) race and corrupt each other's results.
+ *     Serialise them on one stream.
+ *   - Calls no cudaMalloc / cudaFree; enqueues a 4-byte status memset and the
+ *     kernels on `stream`.  The status word is the first int of the array. */
+SI_API size_t si_indexer_topk_noalloc_max_ws_bytes(void);
+SI_API int si_indexer_topk_noalloc(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B,
+                                   int S, int T, int H, int D, int top_k, int causal_ratio,
+                                   const uint8_t* causal_mask, int64_t* out_idx, float* out_scores,
+                                   cudaStream_t stream);
+
 /* Materialised indexer scores, no mask.
  * Replaces indexer_score (flash_sparse/triton/indexer_score.py:123-179).
  *   out [B,S,T] fp32.  ws: at least 256 bytes (status word). */

@@ -29,6 +29,9 @@ SIGNATURES = {
                                    c_int, c_int, c_void_p, ctypes.c_longlong, ctypes.c_uint, c_void_p, c_void_p,
                                    c_void_p, c_size_t, c_void_p]),
     "si_topk_row_sort": (c_int, [c_void_p, c_void_p, ctypes.c_longlong, c_int, c_void_p]),
+    "si_indexer_topk_noalloc_max_ws_bytes": (c_size_t, []),
+    "si_indexer_topk_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                        c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "si_indexer_score": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_size_t, c_void_p]),
 }

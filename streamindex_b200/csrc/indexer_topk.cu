@@ -1,6 +1,7 @@
 // Fused indexer score + streaming top-k kernel, row-sort kernel and launchers.
 // Design notes are in indexer_topk.cuh.
 #include <cstdio>
+#include <mutex>
 #include <cuda_bf16.h>
 
 #include "indexer_topk.cuh"
@@ -772,6 +773,78 @@ int si_indexer_score(const void* q, const void* k, const void* w, int w_is_bf16,
   if (!out) return si::fail("indexer_score: null output pointer");
   return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, 1, 0, nullptr, si::kModeScore, nullptr, out,
                          ws, ws_bytes, stream);
+}
+
+}  // extern "C"
+
+// ==================================================================== allocation-free variant
+// For callers that cannot allocate device memory themselves (for example a
+// host runtime that owns the device allocator and forbids cudaMalloc from
+// plugins, or code that must not allocate while a latency-critical stream is
+// running): the workspace lives in this file-scope device array instead of a
+// caller buffer.  Every GPU that loads the library holds the array until the
+// process exits.
+namespace si {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device, resolved once per device with
+// that device current (the host-side symbol is not a device address).
+static void* noalloc_scratch_ptr(int* rc) {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *rc = fail_cuda("indexer_topk_noalloc: cudaGetDevice", e);
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    *rc = fail("indexer_topk_noalloc: device ordinal %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *rc = fail_cuda("indexer_topk_noalloc: cudaGetSymbolAddress", e);
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *rc = 0;
+  return ptrs[dev];
+}
+
+}  // namespace si
+
+extern "C" {
+
+size_t si_indexer_topk_noalloc_max_ws_bytes(void) { return si::kNoAllocScratchBytes; }
+
+int si_indexer_topk_noalloc(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S,
+                            int T, int H, int D, int top_k, int causal_ratio, const uint8_t* causal_mask,
+                            int64_t* out_idx, float* out_scores, cudaStream_t stream) {
+  if (top_k < 1 || top_k > 2048) return si::fail("indexer_topk_noalloc: top_k must be in [1, 2048] (got %d)", top_k);
+  if (!out_idx || !out_scores) return si::fail("indexer_topk_noalloc: null output pointer");
+  if (H != 16 && H != 32 && H != 64 && H != 128)
+    return si::fail("indexer_topk_noalloc: H_I must be 16, 32, 64 or 128 (got %d)", H);
+  const size_t need = si::indexer_ws_bytes(B < 1 ? 1 : B, S < 1 ? 1 : S, H, top_k);
+  if (need > si::kNoAllocScratchBytes)
+    return si::fail(
+        "indexer_topk_noalloc: needs %zu bytes of scratch, above the built-in maximum of %zu bytes "
+        "(smaller H_I*top_k per SM fits; otherwise use si_indexer_topk with a caller workspace)",
+        need, si::kNoAllocScratchBytes);
+  int rc = 0;
+  void* ws = si::noalloc_scratch_ptr(&rc);
+  if (!ws) return rc;
+  // run_indexer zeroes the status word on `stream`; the candidate buffers need
+  // no clearing (per-query counts start at zero in shared memory).
+  const int mode = causal_ratio > 0 ? si::kModeTopk : (causal_mask ? si::kModeTopkMask : si::kModeTopk);
+  return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, top_k, causal_ratio > 0 ? causal_ratio : 0,
+                         causal_mask, mode, out_idx, out_scores, ws, si::kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"
