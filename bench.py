@@ -301,8 +301,8 @@ def run_ours(a, world, rank, local):
     achieved_tf = flops / (k_ms * 1e-3) / 1e12
     tr = load_traffic()
     traffic = None
-    if tr and tr.get("S") and tr.get("bytes_per_legal_pair"):
-        traffic = tr["bytes_per_legal_pair"] * legal_pairs(a.S, T, a.ratio, s_lo, s_hi)
+    if tr and tr.get("bytes_per_query") and a.H == 64 and a.D == 128 and a.k == 512:
+        traffic = tr["bytes_per_query"] * n_loc  # ncu capture scaled by queries per launch
     sort_bytes = n_loc * a.k * (8 + 8 + 4)
     sort_gbs = sort_bytes / (s_ms * 1e-3) / 1e9
     hbm_peak = peaks.get("hbm_gbs") or 6650.0
