@@ -101,6 +101,21 @@ SI_API int si_indexer_topk_noalloc(const void* q, const void* k, const void* w, 
 SI_API int si_indexer_score(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
                      int H, int D, float* out, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+/* Sparse MQA attention forward with attention sink.
+ * Replaces sparse_attn_fwd (flash_sparse/triton/sparse_attn_fwd.py:180-292) and
+ * the math of reference_sparse_attn (flash_sparse/reference.py:44-130).
+ *   q          [B,S,H,D]   bf16        D % 8 == 0
+ *   kv         [B,Nkv,D]   bf16        one shared KV head
+ *   attn_sink  [H]         fp32        enters the softmax denominator only
+ *   topk_idxs  [B,S,K]     int32       row of kv per slot; -1 (or >= Nkv) = masked
+ *   o          [B,S,H,Dv]  bf16        o = softmax(scale * q.kv^T) . kv[..., :Dv]
+ *   lse        [B,S,H]     fp32 (nullable)  log(sum exp + exp(sink)); -1e30 if empty
+ *   Dv: value width, a multiple of 64 and <= D (512 for the 576/512 MLA layout,
+ *       D for the reference's full-width output).  ws: >= 256 bytes. */
+SI_API int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B,
+                              int S, int H, int D, int Nkv, int K, int Dv, float softmax_scale, void* o, float* lse,
+                              void* ws, size_t ws_bytes, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

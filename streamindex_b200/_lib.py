@@ -32,6 +32,8 @@ SIGNATURES = {
     "si_indexer_topk_noalloc_max_ws_bytes": (c_size_t, []),
     "si_indexer_topk_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "si_sparse_attn_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                   c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "si_indexer_score": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_size_t, c_void_p]),
 }

@@ -1,0 +1,93 @@
+"""Sparse MQA attention forward with attention sink, over the C ABI.
+
+* :func:`sparse_attn_fwd` — ``flash_sparse/triton/sparse_attn_fwd.py:180-292``
+* :func:`sparse_attn`     — ``flash_sparse/triton/__init__.py:50-61`` (autograd
+  wrapper; the backward pass is out of scope and raises ``NotImplementedError``)
+
+Semantics follow ``reference_sparse_attn`` (``flash_sparse/reference.py:44-130``):
+``-1`` indices are masked, the sink enters the denominator only, the default
+scale is ``D**-0.5``, an all-masked query returns 0.  ``d_v`` (new keyword)
+selects the value width: ``None`` returns the reference's full-``D`` output;
+``d_v=512`` on the 576-wide MLA layout equals ``reference_sparse_attn(...)[..., :512]``.
+``block_h`` / ``block_n`` are the reference's Triton tiling knobs, accepted and
+ignored.  Returns ``(o bf16 [B,S,H,d_v], lse fp32 [B,S,H])``.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+
+def sparse_attn_fwd(
+    q: torch.Tensor,
+    kv: torch.Tensor,
+    attn_sink: torch.Tensor,
+    topk_idxs: torch.Tensor,
+    softmax_scale: Optional[float] = None,
+    *,
+    block_h: Optional[int] = None,
+    block_n: int = 64,
+    d_v: Optional[int] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    del block_h, block_n  # Triton tiling knobs of the reference
+    assert q.is_cuda and kv.is_cuda, "inputs must be CUDA tensors (no CPU fallback)"
+    assert q.dim() == 4 and kv.dim() == 3
+    assert q.dtype == torch.bfloat16, f"q must be bf16, got {q.dtype}"
+    assert kv.dtype == q.dtype
+    assert attn_sink.dtype == torch.float32
+    B, S, H, D = q.shape
+    B2, N_kv, D2 = kv.shape
+    assert B2 == B and D2 == D, "q and kv shape mismatch"
+    assert attn_sink.shape == (H,)
+    assert topk_idxs.shape[:2] == (B, S)
+    K = topk_idxs.shape[-1]
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    dv = D if d_v is None else int(d_v)
+    if not (0 < dv <= D):
+        raise ValueError(f"d_v ({dv}) must be in (0, D={D}]")
+    dev = q.device
+    # widths the kernel takes: value width a multiple of 64; zero-pad the head
+    # dim otherwise (zero columns change no score and are sliced off)
+    dv_k = ((dv + 63) // 64) * 64
+    Dp = max(D, dv_k)
+    Dp = ((Dp + 7) // 8) * 8
+    qk, kvk = q.contiguous(), kv.contiguous()
+    if Dp != D:
+        qk = F.pad(qk, (0, Dp - D))
+        kvk = F.pad(kvk, (0, Dp - D))
+    idx = topk_idxs.to(device=dev, dtype=torch.int32).contiguous()
+    sink = attn_sink.to(device=dev).contiguous()
+    o = torch.empty((B, S, H, dv_k), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, S, H), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(256, dtype=torch.uint8, device=dev)
+        _lib.check(lib.si_sparse_attn_fwd(
+            qk.data_ptr(), kvk.data_ptr(), sink.data_ptr(), idx.data_ptr() if K > 0 else None, B, S, H, Dp, N_kv, K,
+            dv_k, float(softmax_scale), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, _lib.stream_handle(dev)))
+        _lib.maybe_check_status(ws, dev, "sparse_attn_fwd")
+    if dv_k != dv:
+        o = o[..., :dv].contiguous()
+    return o, lse
+
+
+class _SparseAttnFunc(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, kv, attn_sink, topk_idxs, softmax_scale, d_v):
+        o, _ = sparse_attn_fwd(q, kv, attn_sink, topk_idxs, softmax_scale, d_v=d_v)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        raise NotImplementedError("sparse attention backward is not part of this build (forward only)")
+
+
+def sparse_attn(q, kv, attn_sink, topk_idxs, softmax_scale: Optional[float] = None, *, d_v: Optional[int] = None):
+    """Forward of the reference's differentiable ``sparse_attn``; returns ``o`` only."""
+    return _SparseAttnFunc.apply(q, kv, attn_sink, topk_idxs, softmax_scale, d_v)

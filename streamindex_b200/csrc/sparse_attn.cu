@@ -85,3 +85,433 @@ __host__ __device__ inline size_t smem_bytes(int NA) {
 
 }  // namespace attn
 }  // namespace si
+
+namespace si {
+namespace attn {
+
+// Index of a kv row for the gather, or an out-of-range row (zero-filled by
+// TMA) when the slot is masked (-1) or past the end of the index list.
+__device__ __forceinline__ int gather_row(const Params& p, int b, int s, int kk, bool& valid) {
+  int v = -1;
+  if (kk < p.K) v = p.idx[((size_t)b * p.S + s) * p.K + kk];
+  valid = v >= 0 && v < p.Nkv;
+  return valid ? b * p.Nkv + v : p.B * p.Nkv;
+}
+
+// Softmax / correction / output warps (warps 2-5).  Warp quarter qd owns
+// head rows 16*qd .. 16*qd+15 of the 64-head group: lane 16+i holds row i of
+// S (32x32b TMEM load) and runs its online softmax; lane i owns the same
+// row of O (16x32bx2 TMEM shape: lanes 0-15 of the quarter, columns split
+// between the two half-warps).
+template <int NK, int DVH>
+__device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t* sP, uint32_t tmem, int warp,
+                                             uint32_t lane, int nitems, int ntiles) {
+  constexpr float kLn2 = 0.6931471805599453f;
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int qd = warp & 3;
+  const int r = (int)(lane & 15);          // row within the quarter
+  const bool srow = lane >= 16;            // this lane holds an S row
+  const int hrow = 16 * qd + r;            // row within the 64-head group
+  const uint32_t tq = tmem + ((uint32_t)(32 * qd) << 16);
+  volatile int* abort_flag = &ms->abort_flag;
+  uint32_t sf[2] = {0, 0}, pvph = 0;
+
+  for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
+    const int hg = it % p.hgroups;
+    const int bs = it / p.hgroups;
+    const int b = bs / p.S, s = bs % p.S;
+    const int head = hg * kHeads + hrow;
+    const float sink2 = head < p.H ? p.sink[head] * kLog2e : 0.f;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      bool valid;
+      gather_row(p, b, s, t * NK + (int)lane, valid);
+      const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+      if (!mbar_wait(&ms->s_full[t & 1], sf[t & 1], abort_flag, p.status, kErrWaitAccFull)) {
+        ok = false;
+        break;
+      }
+      sf[t & 1] ^= 1;
+      tc_fence_after();
+      float sv[NK];
+      tmem_ld32_sync(tq + (t & 1) * NK, sv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ms->s_free[t & 1]);
+
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < NK; ++j) {
+        sv[j] = ((vmask >> j) & 1u) ? sv[j] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, sv[j]);
+      }
+      bool rescale = false;
+      float alpha = 1.f;
+      if (mt > -INFINITY) {
+        if (m_used == -INFINITY) {
+          m_used = mt;  // nothing accumulated yet for this row: O row is zero
+        } else if (mt > m_used + 8.f) {
+          alpha = exp2f(m_used - mt);
+          m_used = mt;
+          l *= alpha;
+          rescale = true;
+        }
+      }
+      float psum = 0.f;
+#pragma unroll
+      for (int j = 0; j < NK; ++j) {
+        sv[j] = (m_used == -INFINITY) ? 0.f : exp2f(sv[j] - m_used);
+        psum += sv[j];
+      }
+      l += psum;
+
+      if (t >= 1) {
+        // MMA2 of the previous tile must be done before O is rescaled and
+        // before this P buffer (last read two tiles ago) is overwritten.
+        if (!mbar_wait(&ms->pv_done, pvph, abort_flag, p.status, kErrWaitAccFull)) {
+          ok = false;
+          break;
+        }
+        pvph ^= 1;
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, rescale && srow)) {
+        const float a_row = __shfl_sync(0xffffffffu, srow ? alpha : 1.f, 16 + r);
+#pragma unroll 1
+        for (int c = 0; c < DVH / 32; ++c) {
+          float v[32];
+          tmem_ld16x32bx2_x32_sync<DVH>(tq + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= a_row;
+          tmem_st16x32bx2_x32<DVH>(tq + c * 32, v);
+        }
+        tmem_st_wait();
+      }
+      if (srow) {
+        uint8_t* prow = sP + (t & 1) * NK * 128 + (hrow >> 3) * 128 + (hrow & 7) * 16;
+#pragma unroll
+        for (int kc = 0; kc < NK / 8; ++kc) {
+          uint4 u;
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(sv[kc * 8 + 0], sv[kc * 8 + 1]);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(sv[kc * 8 + 2], sv[kc * 8 + 3]);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(sv[kc * 8 + 4], sv[kc * 8 + 5]);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(sv[kc * 8 + 6], sv[kc * 8 + 7]);
+          u.x = *reinterpret_cast<uint32_t*>(&h0);
+          u.y = *reinterpret_cast<uint32_t*>(&h1);
+          u.z = *reinterpret_cast<uint32_t*>(&h2);
+          u.w = *reinterpret_cast<uint32_t*>(&h3);
+          *reinterpret_cast<uint4*>(prow + kc * 1024) = u;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ms->p_full[t & 1]);
+    }
+    if (!ok) break;
+    if (!mbar_wait(&ms->pv_done, pvph, abort_flag, p.status, kErrWaitAccFull)) break;
+    pvph ^= 1;
+    tc_fence_after();
+
+    // ---- epilogue: sink in the denominator, normalise, write O and LSE
+    if (m_used == -INFINITY) m_used = sink2;  // no valid key: O = 0, l = exp(sink - sink)
+    const float l_tot = l + exp2f(sink2 - m_used);
+    const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+    if (srow && head < p.H && p.lse)
+      p.lse[(size_t)bs * p.H + head] = l_tot > 0.f ? (m_used + log2f(l_tot)) * kLn2 : -1.0e30f;
+    const float inv_row = __shfl_sync(0xffffffffu, inv, 16 + r);
+    __nv_bfloat16* orow = p.o + ((size_t)bs * p.H + head) * p.o_ld + p.o_off + (lane >> 4) * DVH;
+#pragma unroll 1
+    for (int c = 0; c < DVH / 32; ++c) {
+      float v[32];
+      tmem_ld16x32bx2_x32_sync<DVH>(tq + c * 32, v);
+      if (head < p.H) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 u;
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j + 0] * inv_row, v[j + 1] * inv_row);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2] * inv_row, v[j + 3] * inv_row);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4] * inv_row, v[j + 5] * inv_row);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6] * inv_row, v[j + 7] * inv_row);
+          u.x = *reinterpret_cast<uint32_t*>(&h0);
+          u.y = *reinterpret_cast<uint32_t*>(&h1);
+          u.z = *reinterpret_cast<uint32_t*>(&h2);
+          u.w = *reinterpret_cast<uint32_t*>(&h3);
+          *reinterpret_cast<uint4*>(orow + c * 32 + j) = u;
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms->o_free);
+  }
+}
+
+template <int NK, int DVH>
+__global__ void __launch_bounds__(kThreads, 1)
+    sparse_attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
+                           Params p) {
+  static_assert(NK == 32, "one index per lane per tile");
+  constexpr int DV = 2 * DVH;
+  constexpr int NMMA = DV < 256 ? DV : 256;  // UMMA N of the PV product
+  constexpr int NCH = DV / NMMA;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NA = p.NA;
+  const int NST = num_stages<NK>(NA);
+  const int SB = stage_bytes<NK>(NA);
+  uint8_t* sQ = smem;                                   // [NA][64 rows][128 B], 128B swizzle
+  uint8_t* sKV = sQ + NA * kHeads * 128;                // [NST][NA][NK rows][128 B], 128B swizzle
+  uint8_t* sP = sKV + (size_t)NST * SB;                 // [2][NK/8][8 row groups][8 rows][16 B]
+  Misc* ms = reinterpret_cast<Misc*>(sP + 2 * NK * 128);
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t lane = lane_id();
+  const int nitems = p.B * p.S * p.hgroups;
+  const int ntiles = p.K > 0 ? (p.K + NK - 1) / NK : 1;
+  volatile int* abort_flag = &ms->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&ms->kv_full[i], 1);
+      mbar_init(&ms->kv_empty[i], 1);
+    }
+    mbar_init(&ms->q_full, 1);
+    mbar_init(&ms->q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ms->s_full[i], 1);
+      mbar_init(&ms->s_free[i], 4);
+      mbar_init(&ms->p_full[i], 4);
+    }
+    mbar_init(&ms->pv_done, 1);
+    mbar_init(&ms->o_free, 4);
+    ms->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&map_q);
+    prefetch_tmap(&map_kv);
+  }
+  if (warp == 1) {
+    tmem_alloc(&ms->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ms->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer: Q + row gathers
+    uint32_t st = 0, kph = 0, qph = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      const int hg = it % p.hgroups;
+      const int bs = it / p.hgroups;
+      const int b = bs / p.S, s = bs % p.S;
+      if (!mbar_wait(&ms->q_empty, qph ^ 1, abort_flag, p.status, kErrWaitQ)) break;
+      qph ^= 1;
+      if (lane == 0) {
+        mbar_expect_tx(&ms->q_full, (uint32_t)NA * kHeads * 128);
+        const int qrow = bs * p.H + hg * kHeads;
+        for (int a = 0; a < NA; ++a) tma_load_2d(sQ + a * kHeads * 128, &map_q, &ms->q_full, a * 64, qrow);
+      }
+      for (int t = 0; t < ntiles; ++t) {
+        bool valid;
+        const int row = gather_row(p, b, s, t * NK + (int)lane, valid);
+        if (!mbar_wait(&ms->kv_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) mbar_expect_tx(&ms->kv_full[st], (uint32_t)SB);
+        uint8_t* dst = sKV + (size_t)st * SB;
+#pragma unroll
+        for (int g4 = 0; g4 < NK / 4; ++g4) {
+          const int r0 = __shfl_sync(0xffffffffu, row, 4 * g4 + 0);
+          const int r1 = __shfl_sync(0xffffffffu, row, 4 * g4 + 1);
+          const int r2 = __shfl_sync(0xffffffffu, row, 4 * g4 + 2);
+          const int r3 = __shfl_sync(0xffffffffu, row, 4 * g4 + 3);
+          if (lane == 0)
+            for (int a = 0; a < NA; ++a)
+              tma_gather4(dst + a * NK * 128 + g4 * 4 * 128, &map_kv, &ms->kv_full[st], a * 64, r0, r1, r2, r3);
+        }
+        __syncwarp();
+        if (++st == (uint32_t)NST) {
+          st = 0;
+          kph ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      const uint32_t idesc1 = umma_idesc_f16(kHeads, NK, 1);
+      const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, 1) | (1u << 16);  // B (V) MN-major
+      uint32_t st = 0, kph = 0, qph = 0, pvst = 0;
+      uint32_t sfr[2] = {0, 0}, pf[2] = {0, 0}, ofr = 0;
+      bool ok = true;
+      auto pv = [&](int j, uint32_t stj) -> bool {
+        if (!mbar_wait(&ms->p_full[j & 1], pf[j & 1], abort_flag, p.status, kErrWaitAccFull)) return false;
+        pf[j & 1] ^= 1;
+        if (j == 0) {
+          if (!mbar_wait(&ms->o_free, ofr ^ 1, abort_flag, p.status, kErrWaitAccEmpty)) return false;
+          ofr ^= 1;
+        }
+        tc_fence_after();
+        const uint32_t pbase = smem_u32(sP + (j & 1) * NK * 128);
+        const uint32_t vbase = smem_u32(sKV + (size_t)stj * SB) + (p.dv_off / 64) * NK * 128;
+#pragma unroll
+        for (int kk = 0; kk < NK / 16; ++kk) {
+          const uint64_t adesc = umma_desc(pbase + kk * 2048, 1024, 128, 0);
+#pragma unroll
+          for (int nh = 0; nh < NCH; ++nh) {
+            const uint64_t bdesc = umma_desc(vbase + nh * (NMMA / 64) * NK * 128 + kk * 2048, NK * 128, 1024, 2);
+            umma_f16(tmem + nh * NMMA, adesc, bdesc, idesc2, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&ms->pv_done);
+        umma_commit(&ms->kv_empty[stj]);
+        return true;
+      };
+      for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+        if (!mbar_wait(&ms->q_full, qph, abort_flag, p.status, kErrWaitQ)) break;
+        qph ^= 1;
+        tc_fence_after();
+        const uint32_t qbase = smem_u32(sQ);
+        for (int t = 0; t < ntiles; ++t) {
+          if (!mbar_wait(&ms->kv_full[st], kph, abort_flag, p.status, kErrWaitTmaFull) ||
+              !mbar_wait(&ms->s_free[t & 1], sfr[t & 1] ^ 1, abort_flag, p.status, kErrWaitAccEmpty)) {
+            ok = false;
+            break;
+          }
+          sfr[t & 1] ^= 1;
+          tc_fence_after();
+          const uint32_t kvbase = smem_u32(sKV + (size_t)st * SB);
+          const uint32_t d_s = tmem + (16u << 16) + (t & 1) * NK;
+          for (int a = 0; a < NA; ++a) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              umma_f16(d_s, umma_desc_sw128(qbase + a * kHeads * 128 + kk * 32),
+                       umma_desc_sw128(kvbase + a * NK * 128 + kk * 32), idesc1, (a | kk) != 0);
+            }
+          }
+          umma_commit(&ms->s_full[t & 1]);
+          if (t == ntiles - 1) umma_commit(&ms->q_empty);
+          if (t >= 1 && !pv(t - 1, pvst)) {
+            ok = false;
+            break;
+          }
+          pvst = st;
+          if (++st == (uint32_t)NST) {
+            st = 0;
+            kph ^= 1;
+          }
+        }
+        if (!ok || !pv(ntiles - 1, pvst)) break;
+      }
+    }
+  } else {
+    attn_softmax<NK, DVH>(p, ms, sP, tmem, warp, lane, nitems, ntiles);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace attn
+}  // namespace si
+
+// ==================================================================== host side
+namespace si {
+namespace attn {
+
+template <int DVH>
+static cudaError_t launch_t(const CUtensorMap& mq, const CUtensorMap& mkv, const Params& p, int grid,
+                            cudaStream_t stream) {
+  constexpr int NK = 32;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(sparse_attn_fwd_kernel<NK, DVH>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  sparse_attn_fwd_kernel<NK, DVH><<<grid, kThreads, smem_bytes<NK>(p.NA), stream>>>(mq, mkv, p);
+  return cudaGetLastError();
+}
+
+static cudaError_t launch(const CUtensorMap& mq, const CUtensorMap& mkv, const Params& p, int grid,
+                          cudaStream_t stream) {
+  switch (p.Dv) {
+    case 64: return launch_t<32>(mq, mkv, p, grid, stream);
+    case 128: return launch_t<64>(mq, mkv, p, grid, stream);
+    case 256: return launch_t<128>(mq, mkv, p, grid, stream);
+    case 512: return launch_t<256>(mq, mkv, p, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace attn
+}  // namespace si
+
+extern "C" {
+
+int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,
+                       int H, int D, int Nkv, int K, int Dv, float softmax_scale, void* o, float* lse, void* ws,
+                       size_t ws_bytes, cudaStream_t stream) {
+  using namespace si;
+  if (!q || !kv || !attn_sink || !o || !ws) return fail("sparse_attn_fwd: null pointer");
+  if (K > 0 && !topk_idxs) return fail("sparse_attn_fwd: null topk_idxs");
+  if (B < 1 || S < 0 || H < 1 || Nkv < 0 || K < 0) return fail("sparse_attn_fwd: bad sizes");
+  if (D < 8 || D % 8 || D > 1024) return fail("sparse_attn_fwd: D must be a multiple of 8 in [8,1024] (got %d)", D);
+  if (Dv < 64 || Dv % 64 || Dv > ((D + 63) / 64) * 64 || Dv > D)
+    return fail("sparse_attn_fwd: Dv must be a multiple of 64 with Dv <= D (got Dv=%d, D=%d)", Dv, D);
+  if ((((uintptr_t)q) | ((uintptr_t)kv) | ((uintptr_t)o)) & 15) return fail("sparse_attn_fwd: 16-byte alignment");
+  if (ws_bytes < kStatusBytes) return fail("sparse_attn_fwd: workspace must hold at least 256 bytes");
+  if ((long long)B * S * H + 64 >= (1ll << 31) || (long long)B * Nkv + 1 >= (1ll << 31))
+    return fail("sparse_attn_fwd: sizes exceed the 2^31 TMA coordinate range");
+  const int NA = (D + 63) / 64;
+  if (attn::num_stages<32>(NA) < 2) return fail("sparse_attn_fwd: D=%d too large for the shared-memory plan", D);
+  int* status = reinterpret_cast<int*>(ws);
+  if (cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream)) return fail_cuda("sparse_attn_fwd: status", e);
+  if (S == 0) return 0;
+
+  CUtensorMap mq, mkv;
+  if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, attn::kHeads, 0)) return rc;
+  if (int rc = make_tmap_2d_16b(&mkv, kv, D, (uint64_t)B * (Nkv > 0 ? Nkv : 1), 64, 1, 0)) return rc;
+
+  attn::Params p{};
+  p.B = B; p.S = S; p.H = H; p.D = D; p.NA = NA; p.Nkv = Nkv; p.K = K;
+  p.o_ld = Dv;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.idx = topk_idxs;
+  p.sink = attn_sink;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.status = status;
+  p.hgroups = (H + attn::kHeads - 1) / attn::kHeads;
+  const long long items = (long long)B * S * p.hgroups;
+  const int sms = device_sm_count();
+  const int grid = (int)(items < sms ? items : sms);
+  // value columns in passes of 512 / 256 / 128 / 64 (TMEM holds at most 512 fp32 columns)
+  int done = 0;
+  while (done < Dv) {
+    int pass = 512;
+    while (pass > Dv - done) pass >>= 1;
+    p.Dv = pass;
+    p.dv_off = done;
+    p.o_off = done;
+    p.lse = done == 0 ? lse : nullptr;
+    cudaError_t e = attn::launch(mq, mkv, p, grid, stream);
+    if (e != cudaSuccess) return fail_cuda("sparse_attn_fwd: kernel launch", e);
+    done += pass;
+  }
+  return 0;
+}
+
+}  // extern "C"

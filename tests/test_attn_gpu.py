@@ -1,0 +1,62 @@
+"""GPU parity: sparse attention forward against the CPU oracle and the
+reference golden fixtures.  Tolerance (north star): output atol 2e-2; LSE
+atol 1e-3 (fp32)."""
+
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(q, kv, sink, idx, d_v=None, scale=None):
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    o, lse = sparse_attn_fwd(q.cuda(), kv.cuda(), sink.cuda(), idx.cuda(), scale, d_v=d_v)
+    torch.cuda.synchronize()
+    ro, rl = oracle.sparse_attn(q, kv, sink, idx, scale, d_v=d_v)
+    o = o.float().cpu()
+    assert o.shape == ro.shape
+    err = (o - ro).abs().max().item()
+    assert err <= 2e-2, err
+    assert oracle.norm_corr(o, ro) < 5e-3
+    torch.testing.assert_close(lse.cpu(), rl, atol=1e-3, rtol=1e-4)
+    return o, ro
+
+
+@pytest.mark.parametrize("name", ["attn_576", "attn_128"])
+def test_sparse_attn_golden(golden, name):
+    d = golden(name)
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    o, _ = sparse_attn_fwd(d["q"].cuda(), d["kv"].cuda(), d["sink"].cuda(), d["idx"].cuda())
+    assert (o.float().cpu() - d["o"]).abs().max().item() <= 2e-2
+
+
+def test_mla_576_512_config4_shape():
+    """Config-4 layout at small S: H=64, D=576, value = first 512 dims, K=512."""
+    q, kv, sink, idx = oracle.attn_inputs(1, 96, 64, 576, 2048, 512, ratio=1, seed=0)
+    _check(q, kv, sink, idx, d_v=512)
+
+
+def test_causal_random_idx_zero_sink():
+    q, kv, sink, idx = oracle.attn_inputs(1, 200, 64, 576, 64, 64, ratio=4, seed=1, sink="zeros")
+    _check(q, kv, sink, idx, d_v=512)
+
+
+@pytest.mark.parametrize("H,D,K", [(16, 128, 40), (128, 128, 70), (64, 512, 96), (8, 64, 17)])
+def test_heads_dims_and_ragged_k(H, D, K):
+    q, kv, sink, idx = oracle.attn_inputs(2, 33, H, D, 150, K, ratio=1, seed=H + D)
+    idx[:, :, 3::4] = -1            # every 4th slot masked
+    idx[0, 5] = -1                  # one all-masked query -> output 0
+    o, ro = _check(q, kv, sink, idx)
+    assert o[0, 5].abs().max().item() < 1e-3
+
+
+def test_large_score_range_rescales():
+    """Scores growing along the index list force the running-shift rescale."""
+    q, kv, sink, idx = oracle.attn_inputs(1, 8, 64, 128, 512, 256, ratio=1, seed=5)
+    kv = (kv.float() * torch.linspace(0.1, 6.0, 512).view(1, -1, 1)).to(torch.bfloat16)
+    idx = torch.arange(256, dtype=torch.int32).view(1, 1, -1).expand(1, 8, 256).contiguous() * 2
+    _check(q * 8, kv, sink, idx)
