@@ -10,7 +10,7 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-def _check(q, kv, sink, idx, d_v=None, scale=None):
+def _check(q, kv, sink, idx, d_v=None, scale=None, rtol=0.0):
     from streamindex_b200.attention import sparse_attn_fwd
 
     o, lse = sparse_attn_fwd(q.cuda(), kv.cuda(), sink.cuda(), idx.cuda(), scale, d_v=d_v)
@@ -18,7 +18,7 @@ def _check(q, kv, sink, idx, d_v=None, scale=None):
     ro, rl = oracle.sparse_attn(q, kv, sink, idx, scale, d_v=d_v)
     o = o.float().cpu()
     assert o.shape == ro.shape
-    err = (o - ro).abs().max().item()
+    err = ((o - ro).abs() - rtol * ro.abs()).max().item()
     assert err <= 2e-2, err
     assert oracle.norm_corr(o, ro) < 5e-3
     torch.testing.assert_close(lse.cpu(), rl, atol=1e-3, rtol=1e-4)
@@ -59,4 +59,5 @@ def test_large_score_range_rescales():
     q, kv, sink, idx = oracle.attn_inputs(1, 8, 64, 128, 512, 256, ratio=1, seed=5)
     kv = (kv.float() * torch.linspace(0.1, 6.0, 512).view(1, -1, 1)).to(torch.bfloat16)
     idx = torch.arange(256, dtype=torch.int32).view(1, 1, -1).expand(1, 8, 256).contiguous() * 2
-    _check(q * 8, kv, sink, idx)
+    # outputs reach ~18 here, where one bf16 ulp is 0.125: allow 1% relative on top of atol
+    _check(q * 8, kv, sink, idx, rtol=1e-2)
