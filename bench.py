@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-queries", type=int, default=96)
     ap.add_argument("--no-gather", action="store_true")
+    ap.add_argument("--workload", default="indexer", choices=["indexer", "attn"],
+                    help="indexer: the headline metric (default); attn: BASELINE configs[3] sparse attention")
     return ap.parse_args()
 
 
@@ -403,8 +405,102 @@ def run_cpu_baseline(a, q, k, w, s_lo):
                        f"(eval/test_v4_indexer_parity.py:111-137 restated), {t:.2f} s, torch threads={threads}")}
 
 
+def gen_attn_idx(S, K, n_kv, ratio, device, seed=0, chunk=4096):
+    """Per query, min(K, (s+1)//ratio) distinct indices drawn uniformly from [0, (s+1)//ratio), -1 padded."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = torch.full((1, S, K), -1, dtype=torch.int32, device=device)
+    t = torch.arange(n_kv, device=device)
+    for s0 in range(0, S, chunk):
+        s1 = min(S, s0 + chunk)
+        lim = torch.clamp((torch.arange(s0, s1, device=device) + 1) // ratio, max=n_kv)
+        r = torch.rand((s1 - s0, n_kv), generator=g, device=device)
+        r = r.masked_fill(t.unsqueeze(0) >= lim.unsqueeze(1), -1.0)
+        v, i = r.topk(K, dim=-1)
+        out[0, s0:s1] = torch.where(v >= 0, i, torch.full_like(i, -1)).to(torch.int32)
+    return out
+
+
+def run_attn(a):
+    """sparse attention forward, B=1, S=65536, H=64, D=576/512, N_kv=16384, K=512."""
+    from streamindex_b200 import _lib
+
+    S, H, D, DV, NKV, K = a.S, 64, 576, 512, 16384, 512
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    q = torch.randn((1, S, H, D), generator=g, device=device, dtype=torch.bfloat16).mul_(D ** -0.5)
+    kv = torch.randn((1, NKV, D), generator=g, device=device, dtype=torch.bfloat16)
+    sink = torch.zeros(H, dtype=torch.float32, device=device)
+    idx = gen_attn_idx(S, K, NKV, 4, device)
+    o = torch.empty((1, S, H, DV), dtype=torch.bfloat16, device=device)
+    lse = torch.empty((1, S, H), dtype=torch.float32, device=device)
+    ws = torch.empty(256, dtype=torch.uint8, device=device)
+    lib = _lib.load()
+    st = _lib.stream_handle(device)
+
+    def step():
+        _lib.check(lib.si_sparse_attn_fwd(q.data_ptr(), kv.data_ptr(), sink.data_ptr(), idx.data_ptr(), 1, S, H, D,
+                                          NKV, K, DV, D ** -0.5, o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, st))
+
+    for _ in range(a.warmup):
+        step()
+    assert _lib.read_status(ws, device) == 0
+    clocks = ClockSampler(0)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / a.steps
+    V = int((idx >= 0).sum().item())
+    flops = 2.0 * H * V * (D + DV)
+    gather_bytes = V * D * 2
+    uniq = q.numel() * 2 + o.numel() * 2 + idx.numel() * 4 + kv.numel() * 2 + lse.numel() * 4
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tf_peak = peaks.get("bf16_tflops", 1590.0)
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    tf = flops / (ms * 1e-3) / 1e12
+    # CPU oracle on a small sample of the same queries
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    n = 8
+    pos = torch.linspace(0, S - 1, n).long()
+    t = time.perf_counter()
+    oracle.sparse_attn(q[:, pos.to(device)].cpu(), kv.cpu(), sink.cpu(), idx[:, pos.to(device)].cpu(), D ** -0.5,
+                       d_v=DV)
+    cpu_s = time.perf_counter() - t
+    line = {
+        "metric": "sparse attention forward (BASELINE configs[3]) Mqueries/s", "value": S / (ms * 1e-3) / 1e6,
+        "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; causal uniform indices without replacement)",
+        "config": {"workload": "sparse_attn_fwd B=1 S=%d H=64 D_qk=576 D_v=512 N_kv=16384 K=512" % S,
+                   "valid_slots": V, "l2": "q/o larger than L2; kv (18.9 MB) L2-resident by design"},
+        "gpu_launches": a.steps,
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": tf_peak, "unit": "TFLOP/s", "frac": tf / tf_peak,
+                     "peak_source": "of measured (bf16_tflops burst, MEASURED_PEAKS.json)", "traffic": None,
+                     "hbm_unique_gbs": uniq / (ms * 1e-3) / 1e9, "hbm_frac": uniq / (ms * 1e-3) / 1e9 / hbm_peak,
+                     "gather_gbs_from_l2": gather_bytes / (ms * 1e-3) / 1e9},
+        "cpu_baseline": {"value": n / cpu_s / 1e6, "unit": "Mqueries/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{n} queries, reference_sparse_attn restated (oracle), {cpu_s:.2f} s"},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
+    if a.workload == "attn":
+        if a.S == 1 << 20:
+            a.S = 65536
+        run_attn(a)
+        return
     world, rank, local = init_dist()
     if a.impl == "reference":
         run_reference(a, world, rank)
