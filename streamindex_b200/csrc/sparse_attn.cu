@@ -62,7 +62,7 @@ struct __align__(8) Misc {
   uint64_t q_full, q_empty;
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
-  uint64_t pv_done, o_free;
+  uint64_t pv_done[2], o_free;  // pv_done[b]: MMA2 that read P buffer b completed
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -114,7 +114,20 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
   const int hrow = 16 * qd + r;            // row within the 64-head group
   const uint32_t tq = tmem + ((uint32_t)(32 * qd) << 16);
   volatile int* abort_flag = &ms->abort_flag;
-  uint32_t sf[2] = {0, 0}, pvph = 0;
+  uint32_t sf[2] = {0, 0};
+  // MMA2 of tile j signals pv_done[j & 1]; waited[b] counts completions of
+  // barrier b already consumed, so "MMA2 of tile j is done" is a wait for
+  // completion number (j >> 1) of barrier j & 1 (skipped if already seen).
+  uint32_t waited[2] = {0, 0}, issued_base[2] = {0, 0};
+  auto wait_pv = [&](int j) -> bool {
+    const int bb = j & 1;
+    const uint32_t need = issued_base[bb] + (uint32_t)(j >> 1) + 1;
+    while (waited[bb] < need) {
+      if (!mbar_wait(&ms->pv_done[bb], waited[bb] & 1, &ms->abort_flag, p.status, kErrWaitAccFull)) return false;
+      ++waited[bb];
+    }
+    return true;
+  };
 
   for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
     const int hg = it % p.hgroups;
@@ -166,17 +179,19 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       }
       l += psum;
 
-      if (t >= 1) {
-        // MMA2 of the previous tile must be done before O is rescaled and
-        // before this P buffer (last read two tiles ago) is overwritten.
-        if (!mbar_wait(&ms->pv_done, pvph, abort_flag, p.status, kErrWaitAccFull)) {
-          ok = false;
-          break;
-        }
-        pvph ^= 1;
-        tc_fence_after();
+      // P buffer t&1 was last read by MMA2 of tile t-2; a rescale of O also
+      // needs MMA2 of tile t-1 to be complete.
+      const bool any_rescale = __any_sync(0xffffffffu, rescale && srow);
+      if (t >= 2 && !wait_pv(t - 2)) {
+        ok = false;
+        break;
       }
-      if (__any_sync(0xffffffffu, rescale && srow)) {
+      if (any_rescale && t >= 1 && !wait_pv(t - 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (any_rescale) {
         const float a_row = __shfl_sync(0xffffffffu, srow ? alpha : 1.f, 16 + r);
 #pragma unroll 1
         for (int c = 0; c < DVH / 32; ++c) {
@@ -210,9 +225,10 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       if (lane == 0) mbar_arrive(&ms->p_full[t & 1]);
     }
     if (!ok) break;
-    if (!mbar_wait(&ms->pv_done, pvph, abort_flag, p.status, kErrWaitAccFull)) break;
-    pvph ^= 1;
+    if ((ntiles >= 2 && !wait_pv(ntiles - 2)) || !wait_pv(ntiles - 1)) break;
     tc_fence_after();
+    issued_base[0] += (uint32_t)((ntiles + 1) >> 1);  // MMA2s per buffer in this item
+    issued_base[1] += (uint32_t)(ntiles >> 1);
 
     // ---- epilogue: sink in the denominator, normalise, write O and LSE
     if (m_used == -INFINITY) m_used = sink2;  // no valid key: O = 0, l = exp(sink - sink)
@@ -284,7 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ms->s_free[i], 4);
       mbar_init(&ms->p_full[i], 4);
     }
-    mbar_init(&ms->pv_done, 1);
+    mbar_init(&ms->pv_done[0], 1);
+    mbar_init(&ms->pv_done[1], 1);
     mbar_init(&ms->o_free, 4);
     ms->abort_flag = 0;
     fence_barrier_init();
@@ -370,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16(tmem + nh * NMMA, adesc, bdesc, idesc2, (j > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        umma_commit(&ms->pv_done);
+        umma_commit(&ms->pv_done[j & 1]);
         umma_commit(&ms->kv_empty[stj]);
         return true;
       };
