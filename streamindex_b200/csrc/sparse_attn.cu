@@ -38,7 +38,8 @@ namespace si {
 namespace attn {
 
 constexpr int kHeads = 64;    // UMMA M (heads per work item)
-constexpr int kThreads = 192;
+constexpr int kThreads = 448;
+constexpr int kGatherWarps = 8;   // warps 6-13
 constexpr int kSmemMax = 232448;
 
 struct Params {
@@ -50,12 +51,27 @@ struct Params {
   int o_ld, o_off;     // output row stride (elements) and column offset
   float scale_log2;    // softmax_scale * log2(e)
   const int* idx;      // [B,S,K]
+  const __nv_bfloat16* kv;  // [B,Nkv,D]
   const float* sink;   // [H]
   __nv_bfloat16* o;    // [B,S,H,o_ld]
   float* lse;          // [B,S,H] or null
   int* status;
   int hgroups;         // ceil(H/64)
+  unsigned long long* trace;  // debug builds (SI_ATTN_TRACE) only: per-role timestamps of CTA 0
 };
+
+#ifdef SI_ATTN_TRACE
+// trace layout: [role 0..2][item < 4][tile < 16][point < 8] globaltimer ns
+#define SI_TRACE(role, item, tile, pt)                                                                  \
+  do {                                                                                                  \
+    if (p.trace && blockIdx.x == 0 && (item) < 4 && (tile) < 16)                                        \
+      p.trace[(((role) * 4 + (item)) * 16 + (tile)) * 8 + (pt)] = globaltimer();                         \
+  } while (0)
+#else
+#define SI_TRACE(role, item, tile, pt) \
+  do {                                 \
+  } while (0)
+#endif
 
 struct __align__(8) Misc {
   uint64_t kv_full[8], kv_empty[8];
@@ -134,13 +150,17 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
     const int bs = it / p.hgroups;
     const int b = bs / p.S, s = bs % p.S;
     const int head = hg * kHeads + hrow;
+    const int ii = (it - (int)blockIdx.x) / (int)gridDim.x;
+    const bool tr = (warp == 2 && lane == 16);
     const float sink2 = head < p.H ? p.sink[head] * kLog2e : 0.f;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    bool valid_next;
+    gather_row(p, b, s, (int)lane, valid_next);
     for (int t = 0; t < ntiles; ++t) {
-      bool valid;
-      gather_row(p, b, s, t * NK + (int)lane, valid);
-      const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+      const uint32_t vmask = __ballot_sync(0xffffffffu, valid_next);
+      if (t + 1 < ntiles) gather_row(p, b, s, (t + 1) * NK + (int)lane, valid_next);  // prefetch
+      if (tr) SI_TRACE(2, ii, t, 0);
       if (!mbar_wait(&ms->s_full[t & 1], sf[t & 1], abort_flag, p.status, kErrWaitAccFull)) {
         ok = false;
         break;
@@ -148,7 +168,9 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       sf[t & 1] ^= 1;
       tc_fence_after();
       float sv[NK];
+      if (tr) SI_TRACE(2, ii, t, 1);
       tmem_ld32_sync(tq + (t & 1) * NK, sv);
+      if (tr) SI_TRACE(2, ii, t, 2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ms->s_free[t & 1]);
@@ -172,9 +194,11 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
         }
       }
       float psum = 0.f;
+      // m_used = -inf only while no valid key has been seen; then every p is 0
+      const float shift = (m_used == -INFINITY) ? INFINITY : m_used;
 #pragma unroll
       for (int j = 0; j < NK; ++j) {
-        sv[j] = (m_used == -INFINITY) ? 0.f : exp2f(sv[j] - m_used);
+        sv[j] = ex2_approx(sv[j] - shift);
         psum += sv[j];
       }
       l += psum;
@@ -191,6 +215,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
         break;
       }
       tc_fence_after();
+      if (tr) SI_TRACE(2, ii, t, 3);
       if (any_rescale) {
         const float a_row = __shfl_sync(0xffffffffu, srow ? alpha : 1.f, 16 + r);
 #pragma unroll 1
@@ -208,14 +233,10 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
 #pragma unroll
         for (int kc = 0; kc < NK / 8; ++kc) {
           uint4 u;
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(sv[kc * 8 + 0], sv[kc * 8 + 1]);
-          __nv_bfloat162 h1 = __floats2bfloat162_rn(sv[kc * 8 + 2], sv[kc * 8 + 3]);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(sv[kc * 8 + 4], sv[kc * 8 + 5]);
-          __nv_bfloat162 h3 = __floats2bfloat162_rn(sv[kc * 8 + 6], sv[kc * 8 + 7]);
-          u.x = *reinterpret_cast<uint32_t*>(&h0);
-          u.y = *reinterpret_cast<uint32_t*>(&h1);
-          u.z = *reinterpret_cast<uint32_t*>(&h2);
-          u.w = *reinterpret_cast<uint32_t*>(&h3);
+          u.x = pack_bf16x2(sv[kc * 8 + 0], sv[kc * 8 + 1]);
+          u.y = pack_bf16x2(sv[kc * 8 + 2], sv[kc * 8 + 3]);
+          u.z = pack_bf16x2(sv[kc * 8 + 4], sv[kc * 8 + 5]);
+          u.w = pack_bf16x2(sv[kc * 8 + 6], sv[kc * 8 + 7]);
           *reinterpret_cast<uint4*>(prow + kc * 1024) = u;
         }
       }
@@ -223,6 +244,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ms->p_full[t & 1]);
+      if (tr) SI_TRACE(2, ii, t, 4);
     }
     if (!ok) break;
     if ((ntiles >= 2 && !wait_pv(ntiles - 2)) || !wait_pv(ntiles - 1)) break;
@@ -290,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NST; ++i) {
-      mbar_init(&ms->kv_full[i], 1);
+      mbar_init(&ms->kv_full[i], kGatherWarps * 32);  // one cp.async completion arrival per gather thread
       mbar_init(&ms->kv_empty[i], 1);
     }
     mbar_init(&ms->q_full, 1);
@@ -320,13 +342,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = ms->tmem_base;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer: Q + row gathers
-    uint32_t st = 0, kph = 0, qph = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+    // ------------------------------------------------------------ producer: Q tile (TMA)
+    uint32_t qph = 0;
+    for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
       const int hg = it % p.hgroups;
       const int bs = it / p.hgroups;
-      const int b = bs / p.S, s = bs % p.S;
       if (!mbar_wait(&ms->q_empty, qph ^ 1, abort_flag, p.status, kErrWaitQ)) break;
       qph ^= 1;
       if (lane == 0) {
@@ -334,32 +354,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int qrow = bs * p.H + hg * kHeads;
         for (int a = 0; a < NA; ++a) tma_load_2d(sQ + a * kHeads * 128, &map_q, &ms->q_full, a * 64, qrow);
       }
+      __syncwarp();
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ KV row gathers (cp.async)
+    // A tile is NK rows x NA 128-byte atoms.  One warp instruction copies 4
+    // atom-rows (8 lanes x 16 B each, a full 128-byte segment of one kv row);
+    // the 4 gather warps interleave the NA*8 instructions of a tile.  The
+    // destination applies the 128-byte swizzle (16-byte chunk c of row r goes
+    // to chunk c ^ (r & 7)), the layout the UMMA descriptors expect.
+    const int gw = warp - 6;
+    uint32_t st = 0, kph = 0;
+    const uint32_t c = lane & 7;
+    bool ok = true;
+    for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      const int bs = it / p.hgroups;
+      const int b = bs / p.S, s = bs % p.S;
+      const int ii = (it - (int)blockIdx.x) / (int)gridDim.x;
+      const bool tr = (gw == 0 && lane == 0);
+      bool valid_next;
+      int row_next = gather_row(p, b, s, (int)lane, valid_next);
       for (int t = 0; t < ntiles; ++t) {
-        bool valid;
-        const int row = gather_row(p, b, s, t * NK + (int)lane, valid);
+        const int row = row_next;
+        const int vld = valid_next ? 1 : 0;
+        if (t + 1 < ntiles) row_next = gather_row(p, b, s, (t + 1) * NK + (int)lane, valid_next);
+        if (tr) SI_TRACE(0, ii, t, 0);
         if (!mbar_wait(&ms->kv_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
           ok = false;
           break;
         }
-        if (lane == 0) mbar_expect_tx(&ms->kv_full[st], (uint32_t)SB);
-        uint8_t* dst = sKV + (size_t)st * SB;
-#pragma unroll
-        for (int g4 = 0; g4 < NK / 4; ++g4) {
-          const int r0 = __shfl_sync(0xffffffffu, row, 4 * g4 + 0);
-          const int r1 = __shfl_sync(0xffffffffu, row, 4 * g4 + 1);
-          const int r2 = __shfl_sync(0xffffffffu, row, 4 * g4 + 2);
-          const int r3 = __shfl_sync(0xffffffffu, row, 4 * g4 + 3);
-          if (lane == 0)
-            for (int a = 0; a < NA; ++a)
-              tma_gather4(dst + a * NK * 128 + g4 * 4 * 128, &map_kv, &ms->kv_full[st], a * 64, r0, r1, r2, r3);
+        if (tr) SI_TRACE(0, ii, t, 1);
+        const uint32_t base = smem_u32(sKV + (size_t)st * SB);
+        for (int q = gw; q < NA * 8; q += kGatherWarps) {
+          const int u = q * 4 + (int)(lane >> 3);
+          const int r = u & (NK - 1);
+          const int a = u / NK;
+          const int rv = __shfl_sync(0xffffffffu, row, r);
+          const int vv = __shfl_sync(0xffffffffu, vld, r);
+          const int col = a * 64 + (int)c * 8;
+          const bool in = vv && col < p.D;
+          const __nv_bfloat16* src = in ? p.kv + (size_t)rv * p.D + col : p.kv;
+          cp_async_16(base + a * NK * 128 + r * 128 + ((c ^ (uint32_t)(r & 7)) << 4), src, in ? 16u : 0u);
         }
-        __syncwarp();
+        cp_async_arrive_noinc(&ms->kv_full[st]);
+        if (tr) SI_TRACE(0, ii, t, 2);
+        if (tr) SI_TRACE(0, ii, t, 3);
         if (++st == (uint32_t)NST) {
           st = 0;
           kph ^= 1;
         }
       }
     }
+    cp_async_wait<0>();
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
@@ -368,9 +414,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t st = 0, kph = 0, qph = 0, pvst = 0;
       uint32_t sfr[2] = {0, 0}, pf[2] = {0, 0}, ofr = 0;
       bool ok = true;
+      int ii = 0;
       auto pv = [&](int j, uint32_t stj) -> bool {
         if (!mbar_wait(&ms->p_full[j & 1], pf[j & 1], abort_flag, p.status, kErrWaitAccFull)) return false;
         pf[j & 1] ^= 1;
+        SI_TRACE(1, ii, j, 4);
         if (j == 0) {
           if (!mbar_wait(&ms->o_free, ofr ^ 1, abort_flag, p.status, kErrWaitAccEmpty)) return false;
           ofr ^= 1;
@@ -389,20 +437,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&ms->pv_done[j & 1]);
         umma_commit(&ms->kv_empty[stj]);
+        SI_TRACE(1, ii, j, 5);
         return true;
       };
       for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+        ii = (it - (int)blockIdx.x) / (int)gridDim.x;
         if (!mbar_wait(&ms->q_full, qph, abort_flag, p.status, kErrWaitQ)) break;
         qph ^= 1;
         tc_fence_after();
         const uint32_t qbase = smem_u32(sQ);
         for (int t = 0; t < ntiles; ++t) {
+          SI_TRACE(1, ii, t, 0);
           if (!mbar_wait(&ms->kv_full[st], kph, abort_flag, p.status, kErrWaitTmaFull) ||
               !mbar_wait(&ms->s_free[t & 1], sfr[t & 1] ^ 1, abort_flag, p.status, kErrWaitAccEmpty)) {
             ok = false;
             break;
           }
           sfr[t & 1] ^= 1;
+          // the KV tile was written by cp.async (generic proxy); order it
+          // before the tensor core's (async proxy) reads
+          fence_proxy_async_smem();
           tc_fence_after();
           const uint32_t kvbase = smem_u32(sKV + (size_t)st * SB);
           const uint32_t d_s = tmem + (16u << 16) + (t & 1) * NK;
@@ -414,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           umma_commit(&ms->s_full[t & 1]);
+          SI_TRACE(1, ii, t, 3);
           if (t == ntiles - 1) umma_commit(&ms->q_empty);
           if (t >= 1 && !pv(t - 1, pvst)) {
             ok = false;
@@ -477,6 +532,11 @@ static cudaError_t launch(const CUtensorMap& mq, const CUtensorMap& mkv, const P
 }  // namespace attn
 }  // namespace si
 
+#ifdef SI_ATTN_TRACE
+static unsigned long long* g_attn_trace = nullptr;
+extern "C" SI_API void si_debug_set_attn_trace(unsigned long long* t) { g_attn_trace = t; }
+#endif
+
 extern "C" {
 
 int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,
@@ -508,10 +568,14 @@ int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, co
   p.o_ld = Dv;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.idx = topk_idxs;
+  p.kv = reinterpret_cast<const __nv_bfloat16*>(kv);
   p.sink = attn_sink;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.status = status;
   p.hgroups = (H + attn::kHeads - 1) / attn::kHeads;
+#ifdef SI_ATTN_TRACE
+  p.trace = g_attn_trace;
+#endif
   const long long items = (long long)B * S * p.hgroups;
   const int sms = device_sm_count();
   const int grid = (int)(items < sms ? items : sms);
