@@ -116,6 +116,35 @@ SI_API int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_s
                               int S, int H, int D, int Nkv, int K, int Dv, float softmax_scale, void* o, float* lse,
                               void* ws, size_t ws_bytes, cudaStream_t stream);
 
+/* si_sparse_attn_fwd over a kv split in two tensors, as the CSA layer reads
+ * cat[kv; kv_compressed] (flash_sparse/csa.py:199) without building it:
+ * index v < Nkv reads kv[b, v], index v >= Nkv reads kv2[b, v - Nkv]. */
+SI_API int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2,
+                                  const float* attn_sink, const int32_t* topk_idxs, int B, int S, int H, int D, int K,
+                                  int Dv, float softmax_scale, void* o, float* lse, void* ws, size_t ws_bytes,
+                                  cudaStream_t stream);
+
+/* Top-k of a materialised score matrix [B,S,T] fp32 with the causal limit
+ * t < (s+1)/causal_ratio (<= 0: none); same output contract as si_indexer_topk.
+ * Replaces the masked_fill + topk + post-mask of build_csa_topk_idxs
+ * (flash_sparse/csa.py:55-69) and of indexer_score_topk with a causal mask
+ * (flash_sparse/triton/indexer_score.py:200-205). */
+SI_API size_t si_scores_topk_ws_bytes(int B, int S, int top_k);
+SI_API int si_scores_topk(const float* scores, int B, int S, int T, int top_k, int causal_ratio, int64_t* out_idx,
+                          float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream);
+
+/* CSA attention index list [B,S,n_win+top_k] int32: sliding window then
+ * compressed picks offset by S (-1 kept).  Replaces _build_sliding_window_idxs
+ * (flash_sparse/reference.py:460-475) + the concatenation of
+ * flash_sparse/csa.py:76-83 / :176-179.  comp_idx: [B,S,top_k] int64. */
+SI_API int si_csa_build_idx(const int64_t* comp_idx, int B, int S, int top_k, int n_win, int32_t* out,
+                            cudaStream_t stream);
+
+/* Mean-pool compressor [B,S,C] bf16 -> [B,S/m,C] bf16 (trailing S % m tokens
+ * dropped).  Equals reference_token_compressor(overlap=False) with zero scores
+ * and bias (flash_sparse/reference.py:234-240). */
+SI_API int si_mean_pool(const void* x, int B, int S, int C, int m, void* out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,14 @@ SIGNATURES = {
                                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "si_sparse_attn_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                    c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "si_sparse_attn_fwd_kv2": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
+                                       c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t,
+                                       c_void_p]),
+    "si_scores_topk_ws_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "si_scores_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
+                               c_void_p]),
+    "si_csa_build_idx": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "si_mean_pool": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "si_indexer_score": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_size_t, c_void_p]),
 }

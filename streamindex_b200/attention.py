@@ -23,6 +23,37 @@ import torch.nn.functional as F
 from . import _lib
 
 
+def _attn_call(q, kv, kv2, attn_sink, idx, softmax_scale, dv):
+    """One C-ABI call; kv2 (optional) holds rows Nkv.. of the logical kv."""
+    B, S, H, D = q.shape
+    dev = q.device
+    K = idx.shape[-1]
+    dv_k = ((dv + 63) // 64) * 64
+    Dp = ((max(D, dv_k) + 7) // 8) * 8
+    qk, kvk = q.contiguous(), kv.contiguous()
+    kv2k = None if kv2 is None else kv2.contiguous()
+    if Dp != D:
+        qk = F.pad(qk, (0, Dp - D))
+        kvk = F.pad(kvk, (0, Dp - D))
+        if kv2k is not None:
+            kv2k = F.pad(kv2k, (0, Dp - D))
+    idx = idx.to(device=dev, dtype=torch.int32).contiguous()
+    sink = attn_sink.to(device=dev, dtype=torch.float32).contiguous()
+    o = torch.empty((B, S, H, dv_k), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, S, H), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(256, dtype=torch.uint8, device=dev)
+        _lib.check(lib.si_sparse_attn_fwd_kv2(
+            qk.data_ptr(), kvk.data_ptr(), kvk.shape[1], _lib.ptr(kv2k), 0 if kv2k is None else kv2k.shape[1],
+            sink.data_ptr(), idx.data_ptr() if K > 0 else None, B, S, H, Dp, K, dv_k, float(softmax_scale),
+            o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, _lib.stream_handle(dev)))
+        _lib.maybe_check_status(ws, dev, "sparse_attn_fwd")
+    if dv_k != dv:
+        o = o[..., :dv].contiguous()
+    return o, lse
+
+
 def sparse_attn_fwd(
     q: torch.Tensor,
     kv: torch.Tensor,
@@ -51,30 +82,7 @@ def sparse_attn_fwd(
     dv = D if d_v is None else int(d_v)
     if not (0 < dv <= D):
         raise ValueError(f"d_v ({dv}) must be in (0, D={D}]")
-    dev = q.device
-    # widths the kernel takes: value width a multiple of 64; zero-pad the head
-    # dim otherwise (zero columns change no score and are sliced off)
-    dv_k = ((dv + 63) // 64) * 64
-    Dp = max(D, dv_k)
-    Dp = ((Dp + 7) // 8) * 8
-    qk, kvk = q.contiguous(), kv.contiguous()
-    if Dp != D:
-        qk = F.pad(qk, (0, Dp - D))
-        kvk = F.pad(kvk, (0, Dp - D))
-    idx = topk_idxs.to(device=dev, dtype=torch.int32).contiguous()
-    sink = attn_sink.to(device=dev).contiguous()
-    o = torch.empty((B, S, H, dv_k), dtype=torch.bfloat16, device=dev)
-    lse = torch.empty((B, S, H), dtype=torch.float32, device=dev)
-    lib = _lib.load()
-    with torch.cuda.device(dev):
-        ws = torch.empty(256, dtype=torch.uint8, device=dev)
-        _lib.check(lib.si_sparse_attn_fwd(
-            qk.data_ptr(), kvk.data_ptr(), sink.data_ptr(), idx.data_ptr() if K > 0 else None, B, S, H, Dp, N_kv, K,
-            dv_k, float(softmax_scale), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, _lib.stream_handle(dev)))
-        _lib.maybe_check_status(ws, dev, "sparse_attn_fwd")
-    if dv_k != dv:
-        o = o[..., :dv].contiguous()
-    return o, lse
+    return _attn_call(q, kv, None, attn_sink, topk_idxs, softmax_scale, dv)
 
 
 class _SparseAttnFunc(torch.autograd.Function):

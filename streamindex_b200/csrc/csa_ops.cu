@@ -1,0 +1,94 @@
+// CSA glue kernels: sliding-window + compressed index build and the mean-pool
+// compressor.  Both are HBM-bound elementwise passes (grid-stride, coalesced,
+// grid sized to a multiple of the SM count).
+#include <cuda_bf16.h>
+
+#include "capi_common.h"
+#include "../../include/streamindex_b200.h"
+
+namespace si {
+
+// out[b,s,:] = [ window(s) | comp[b,s,j] + S (or -1) ], int32.
+// window(s)_w = s - n_win + 1 + w if that position is in [0, s], else -1
+// (flash_sparse/reference.py:470-475); compressed indices are offset by S
+// because the attention reads cat[kv; kv_compressed] (flash_sparse/csa.py:177-179).
+__global__ void csa_build_idx_kernel(const int64_t* __restrict__ comp, int B, int S, int top_k, int n_win,
+                                     int32_t* __restrict__ out) {
+  const int W = n_win + top_k;
+  const long long total = (long long)B * S * W;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int col = (int)(i % W);
+    const long long bs = i / W;
+    const int s = (int)(bs % S);
+    int v;
+    if (col < n_win) {
+      const int pos = s - n_win + 1 + col;
+      v = (pos >= 0 && pos <= s) ? pos : -1;
+    } else {
+      const long long c = comp[bs * top_k + (col - n_win)];
+      v = c >= 0 ? (int)(c + S) : -1;
+    }
+    out[i] = v;
+  }
+}
+
+// Mean over each block of m tokens: [B,S,C] -> [B,S/m,C] (fp32 math, bf16 out);
+// the non-overlapping compressor with uniform softmax weights
+// (reference_token_compressor(overlap=False), flash_sparse/reference.py:234-240).
+__global__ void mean_pool_kernel(const __nv_bfloat16* __restrict__ x, int B, int S, int C, int m,
+                                 __nv_bfloat16* __restrict__ out) {
+  const int nb = S / m;
+  const int C2 = C / 2;
+  const long long total = (long long)B * nb * C2;
+  const float inv = 1.f / (float)m;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c2 = (int)(i % C2);
+    const long long bn = i / C2;
+    const int n = (int)(bn % nb);
+    const int b = (int)(bn / nb);
+    const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(x + ((long long)b * S + (long long)n * m) * C) + c2;
+    float sx = 0.f, sy = 0.f;
+    for (int j = 0; j < m; ++j) {
+      const float2 f = __bfloat1622float2(src[(long long)j * C2]);
+      sx += f.x * inv;
+      sy += f.y * inv;
+    }
+    reinterpret_cast<__nv_bfloat162*>(out)[i] = __floats2bfloat162_rn(sx, sy);
+  }
+}
+
+static int elementwise_grid(long long n) {
+  const long long blocks = (n + 255) / 256;
+  const long long cap = (long long)device_sm_count() * 16;
+  return (int)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+}  // namespace si
+
+extern "C" {
+
+int si_csa_build_idx(const int64_t* comp_idx, int B, int S, int top_k, int n_win, int32_t* out, cudaStream_t stream) {
+  if (B < 1 || S < 0 || top_k < 0 || n_win < 0) return si::fail("csa_build_idx: bad sizes");
+  if ((long long)S + 1 >= (1ll << 31)) return si::fail("csa_build_idx: S too large for int32 indices");
+  const long long n = (long long)B * S * (n_win + top_k);
+  if (n == 0) return 0;
+  if (!out || (top_k > 0 && !comp_idx)) return si::fail("csa_build_idx: null pointer");
+  si::csa_build_idx_kernel<<<si::elementwise_grid(n), 256, 0, stream>>>(comp_idx, B, S, top_k, n_win, out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : si::fail_cuda("csa_build_idx: launch", e);
+}
+
+int si_mean_pool(const void* x, int B, int S, int C, int m, void* out, cudaStream_t stream) {
+  if (B < 1 || S < 0 || C < 2 || (C & 1) || m < 1) return si::fail("mean_pool: bad sizes (C must be even)");
+  if (((uintptr_t)x | (uintptr_t)out) & 3) return si::fail("mean_pool: 4-byte alignment");
+  const long long n = (long long)B * (S / m) * (C / 2);
+  if (n == 0) return 0;
+  si::mean_pool_kernel<<<si::elementwise_grid(n), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), B, S, C, m, reinterpret_cast<__nv_bfloat16*>(out));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : si::fail_cuda("mean_pool: launch", e);
+}
+
+}  // extern "C"

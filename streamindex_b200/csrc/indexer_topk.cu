@@ -848,3 +848,98 @@ int si_indexer_topk_noalloc(const void* q, const void* k, const void* w, int w_i
 }
 
 }  // extern "C"
+
+// ==================================================================== top-k over a score matrix
+// Top-k of materialised scores [B,S,T] (the non-streaming branch of the CSA
+// index build, flash_sparse/csa.py:55-69): one warp per row streams the row's
+// legal prefix t < limit(s) through the same threshold + candidate-buffer +
+// exact radix-select scheme as the fused kernel, then writes unsorted keys for
+// the row sort.
+namespace si {
+
+constexpr int kRowWarps = 8;
+
+__global__ void __launch_bounds__(32 * kRowWarps)
+    scores_topk_kernel(const float* __restrict__ scores, int B, int S, int T, int ksel, int ratio, int cap,
+                       unsigned long long* cand, unsigned long long* out_keys) {
+  __shared__ uint32_t hist[kRowWarps][256];
+  const int wl = threadIdx.x / 32;
+  const uint32_t lane = lane_id();
+  const uint32_t lt = (1u << lane) - 1u;
+  const long long nwarps = (long long)gridDim.x * kRowWarps;
+  const long long rows = (long long)B * S;
+  unsigned long long* buf = cand + ((long long)blockIdx.x * kRowWarps + wl) * cap;
+  for (long long row = (long long)blockIdx.x * kRowWarps + wl; row < rows; row += nwarps) {
+    const int s = (int)(row % S);
+    int lim = T;
+    if (ratio > 0) {
+      const long long l = ((long long)s + 1) / ratio;
+      lim = l < T ? (int)l : T;
+    }
+    const float* sr = scores + row * (long long)T;
+    unsigned long long thr = 0ull;
+    int cnt = 0;
+    for (int t0 = 0; t0 < lim; t0 += 32) {
+      if (cnt > cap - 32) {
+        thr = warp_select_topk(buf, cnt, ksel, hist[wl]);
+        cnt = ksel;
+      }
+      const int t = t0 + (int)lane;
+      const unsigned long long key = t < lim ? make_key(sr[t], t) : 0ull;
+      const bool pass = t < lim && key > thr;
+      const uint32_t bal = __ballot_sync(0xffffffffu, pass);
+      if (pass) buf[cnt + __popc(bal & lt)] = key;
+      cnt += __popc(bal);
+      __syncwarp();
+    }
+    if (cnt > ksel) {
+      warp_select_topk(buf, cnt, ksel, hist[wl]);
+      cnt = ksel;
+    }
+    unsigned long long* dst = out_keys + row * ksel;
+    for (int x = (int)lane; x < ksel; x += 32) dst[x] = x < cnt ? buf[x] : 0ull;
+    __syncwarp();
+  }
+}
+
+static int scores_topk_grid(long long rows) {
+  const long long want = (rows + kRowWarps - 1) / kRowWarps;
+  const long long maxg = (long long)device_sm_count() * 8;
+  return (int)(want < maxg ? (want > 0 ? want : 1) : maxg);
+}
+
+}  // namespace si
+
+extern "C" {
+
+size_t si_scores_topk_ws_bytes(int B, int S, int top_k) {
+  const long long rows = (long long)(B > 0 ? B : 1) * (S > 0 ? S : 1);
+  return si::kStatusBytes + (size_t)si::scores_topk_grid(rows) * si::kRowWarps * si::pick_cap(top_k > 0 ? top_k : 1) *
+                                sizeof(unsigned long long);
+}
+
+int si_scores_topk(const float* scores, int B, int S, int T, int top_k, int causal_ratio, int64_t* out_idx,
+                   float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (top_k < 1 || top_k > 2048) return si::fail("scores_topk: top_k must be in [1, 2048] (got %d)", top_k);
+  if (B < 1 || S < 0 || T < 0) return si::fail("scores_topk: bad sizes");
+  if ((S > 0 && T > 0 && !scores) || !out_idx || !out_scores || !ws) return si::fail("scores_topk: null pointer");
+  const size_t need = si_scores_topk_ws_bytes(B, S, top_k);
+  if (ws_bytes < need) return si::fail("scores_topk: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  const long long rows = (long long)B * S;
+  if (rows == 0) return 0;
+  if (T == 0) {
+    cudaError_t e = si::launch_fill_pad(out_idx, out_scores, rows * top_k, stream);
+    return e == cudaSuccess ? 0 : si::fail_cuda("scores_topk: pad", e);
+  }
+  const int grid = si::scores_topk_grid(rows);
+  auto* keys = reinterpret_cast<unsigned long long*>(out_idx);
+  si::scores_topk_kernel<<<grid, 32 * si::kRowWarps, 0, stream>>>(
+      scores, B, S, T, top_k, causal_ratio > 0 ? causal_ratio : 0, si::pick_cap(top_k),
+      reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(ws) + si::kStatusBytes), keys);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return si::fail_cuda("scores_topk: launch", e);
+  e = si::launch_row_sort(keys, out_scores, rows, top_k, stream);
+  return e == cudaSuccess ? 0 : si::fail_cuda("scores_topk: row sort", e);
+}
+
+}  // extern "C"

@@ -45,13 +45,15 @@ constexpr int kSmemMax = 232448;
 struct Params {
   int B, S, H, D;      // D: qk head dim (multiple of 8)
   int NA;              // ceil(D/64) swizzle atoms per row
-  int Nkv;             // kv rows per batch
+  int Nkv;             // kv rows per batch (Nkv1 + Nkv2)
+  int Nkv1;            // rows of the first kv tensor; indices >= Nkv1 read kv2
   int K;               // indices per query
   int Dv, dv_off;      // value columns [dv_off, dv_off+Dv) of kv (multiples of 64)
   int o_ld, o_off;     // output row stride (elements) and column offset
   float scale_log2;    // softmax_scale * log2(e)
   const int* idx;      // [B,S,K]
-  const __nv_bfloat16* kv;  // [B,Nkv,D]
+  const __nv_bfloat16* kv;   // [B,Nkv1,D]
+  const __nv_bfloat16* kv2;  // [B,Nkv-Nkv1,D] or null
   const float* sink;   // [H]
   __nv_bfloat16* o;    // [B,S,H,o_ld]
   float* lse;          // [B,S,H] or null
@@ -107,18 +109,21 @@ namespace attn {
 
 // Index of a kv row for the gather, or an out-of-range row (zero-filled by
 // TMA) when the slot is masked (-1) or past the end of the index list.
+// Selected kv index of slot kk of query (b, s), and whether it is a legal row
+// (-1 and indices >= Nkv are masked; slots past K are padding).
 __device__ __forceinline__ int gather_row(const Params& p, int b, int s, int kk, bool& valid) {
   int v = -1;
   if (kk < p.K) v = p.idx[((size_t)b * p.S + s) * p.K + kk];
   valid = v >= 0 && v < p.Nkv;
-  return valid ? b * p.Nkv + v : p.B * p.Nkv;
+  return valid ? v : 0;
 }
 
-// Softmax / correction / output warps (warps 2-5).  Warp quarter qd owns
-// head rows 16*qd .. 16*qd+15 of the 64-head group: lane 16+i holds row i of
-// S (32x32b TMEM load) and runs its online softmax; lane i owns the same
-// row of O (16x32bx2 TMEM shape: lanes 0-15 of the quarter, columns split
-// between the two half-warps).
+// Address of kv row v of batch b in the (possibly split) kv storage.
+__device__ __forceinline__ const __nv_bfloat16* kv_row_ptr(const Params& p, int b, int v) {
+  if (v < p.Nkv1) return p.kv + ((size_t)b * p.Nkv1 + v) * p.D;
+  return p.kv2 + ((size_t)b * (p.Nkv - p.Nkv1) + (v - p.Nkv1)) * p.D;
+}
+
 template <int NK, int DVH>
 __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t* sP, uint32_t tmem, int warp,
                                              uint32_t lane, int nitems, int ntiles) {
@@ -393,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int vv = __shfl_sync(0xffffffffu, vld, r);
           const int col = a * 64 + (int)c * 8;
           const bool in = vv && col < p.D;
-          const __nv_bfloat16* src = in ? p.kv + (size_t)rv * p.D + col : p.kv;
+          const __nv_bfloat16* src = in ? kv_row_ptr(p, b, rv) + col : p.kv;
           cp_async_16(base + a * NK * 128 + r * 128 + ((c ^ (uint32_t)(r & 7)) << 4), src, in ? 16u : 0u);
         }
         cp_async_arrive_noinc(&ms->kv_full[st]);
@@ -539,10 +544,14 @@ extern "C" SI_API void si_debug_set_attn_trace(unsigned long long* t) { g_attn_t
 
 extern "C" {
 
-int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,
-                       int H, int D, int Nkv, int K, int Dv, float softmax_scale, void* o, float* lse, void* ws,
-                       size_t ws_bytes, cudaStream_t stream) {
+int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
+                           const int32_t* topk_idxs, int B, int S, int H, int D, int K, int Dv, float softmax_scale,
+                           void* o, float* lse, void* ws, size_t ws_bytes, cudaStream_t stream) {
   using namespace si;
+  if (Nkv2 < 0 || (Nkv2 > 0 && !kv2)) return fail("sparse_attn_fwd: bad second kv tensor");
+  if (Nkv2 > 0 && (((uintptr_t)kv2) & 15)) return fail("sparse_attn_fwd: 16-byte alignment of kv2");
+  const int Nkv1 = Nkv;
+  Nkv = Nkv1 + Nkv2;
   if (!q || !kv || !attn_sink || !o || !ws) return fail("sparse_attn_fwd: null pointer");
   if (K > 0 && !topk_idxs) return fail("sparse_attn_fwd: null topk_idxs");
   if (B < 1 || S < 0 || H < 1 || Nkv < 0 || K < 0) return fail("sparse_attn_fwd: bad sizes");
@@ -561,7 +570,8 @@ int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, co
 
   CUtensorMap mq, mkv;
   if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, attn::kHeads, 0)) return rc;
-  if (int rc = make_tmap_2d_16b(&mkv, kv, D, (uint64_t)B * (Nkv > 0 ? Nkv : 1), 64, 1, 0)) return rc;
+  if (int rc = make_tmap_2d_16b(&mkv, Nkv1 > 0 ? kv : kv2, D, (uint64_t)B * (Nkv1 > 0 ? Nkv1 : (Nkv2 > 0 ? Nkv2 : 1)), 64, 1, 0))
+    return rc;
 
   attn::Params p{};
   p.B = B; p.S = S; p.H = H; p.D = D; p.NA = NA; p.Nkv = Nkv; p.K = K;
@@ -569,6 +579,8 @@ int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, co
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.idx = topk_idxs;
   p.kv = reinterpret_cast<const __nv_bfloat16*>(kv);
+  p.kv2 = reinterpret_cast<const __nv_bfloat16*>(kv2);
+  p.Nkv1 = Nkv1;
   p.sink = attn_sink;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.status = status;
@@ -593,6 +605,13 @@ int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, co
     done += pass;
   }
   return 0;
+}
+
+int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,
+                       int H, int D, int Nkv, int K, int Dv, float softmax_scale, void* o, float* lse, void* ws,
+                       size_t ws_bytes, cudaStream_t stream) {
+  return si_sparse_attn_fwd_kv2(q, kv, Nkv, nullptr, 0, attn_sink, topk_idxs, B, S, H, D, K, Dv, softmax_scale, o, lse,
+                                ws, ws_bytes, stream);
 }
 
 }  // extern "C"
