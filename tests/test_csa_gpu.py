@@ -69,13 +69,3 @@ def test_flash_csa_forward_small(d_v):
     ro, _, _ = oracle.csa_forward(q, x_kv, kvc.cpu(), q_idx, kc.cpu(), w, sink, nwin, k, m, d_v=d_v)
     assert o.shape == ro.shape
     assert (o.float().cpu() - ro).abs().max().item() <= 2e-2
-
-
-def test_flash_sparse_import_paths():
-    from flash_sparse.csa import flash_csa_forward  # noqa: F401
-    from flash_sparse.triton import sparse_attn, sparse_attn_bwd, sparse_attn_fwd  # noqa: F401
-    from flash_sparse.triton.chunked_indexer import chunked_indexer_topk  # noqa: F401
-    from flash_sparse.triton.indexer_score import indexer_score, indexer_score_topk  # noqa: F401
-
-    with pytest.raises(NotImplementedError):
-        sparse_attn_bwd()
