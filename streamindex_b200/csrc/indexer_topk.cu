@@ -71,8 +71,25 @@ __device__ __forceinline__ void for_each_key(const unsigned long long* buf, int 
 // One warp: keep the `ksel` largest of the n (> ksel) distinct keys in buf,
 // compacted to buf[0, ksel), and return the smallest kept key.  hist is a
 // 256-entry shared scratch owned by this warp.
+#ifdef SI_IDX_TRACE
+__device__ unsigned long long* g_sel_trace = nullptr;  // [event < 4096][point < 8]
+__device__ unsigned int g_sel_count = 0;
+#define SEL_T(pt) do { if (tslot >= 0 && lane == 0) g_sel_trace[tslot * 8 + (pt)] = globaltimer(); } while (0)
+#else
+#define SEL_T(pt) do { } while (0)
+#endif
 __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, int ksel, uint32_t* hist) {
   const uint32_t lane = lane_id();
+#ifdef SI_IDX_TRACE
+  int tslot = -1;
+  if (g_sel_trace && blockIdx.x == 0) {
+    if (lane == 0) tslot = (int)atomicAdd(&g_sel_count, 1u);
+    tslot = __shfl_sync(0xffffffffu, tslot, 0);
+    if (tslot >= 4096) tslot = -1;
+    if (tslot >= 0 && lane == 0) g_sel_trace[tslot * 8 + 7] = (unsigned long long)n;
+  }
+#endif
+  SEL_T(0);
   unsigned long long a = ~0ull, o = 0ull;
   for_each_key(buf, n, lane, [&](unsigned long long k) {
     a &= k;
@@ -83,6 +100,7 @@ __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, i
     a &= shfl_xor_u64(a, m);
     o |= shfl_xor_u64(o, m);
   }
+  SEL_T(1);
   const unsigned long long diff = a ^ o;  // nonzero: keys are distinct and n >= 2
   const int hb = 63 - __clzll((long long)diff);
   unsigned long long mask = (hb == 63) ? 0ull : ~((2ull << hb) - 1ull);
@@ -137,7 +155,11 @@ __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, i
     __syncwarp();
     if ((int)eq == need || shift == 0) break;
     shift = shift >= 8 ? shift - 8 : 0;
+#ifdef SI_IDX_TRACE
+    if (tslot >= 0 && lane == 0) g_sel_trace[tslot * 8 + 6] += 1;  // extra passes
+#endif
   }
+  SEL_T(2);
   // keys >= prefix are exactly the top ksel; compact in place (never writes
   // ahead of the batch being read: all loads of a batch precede its stores)
   const unsigned long long theta = prefix;
@@ -170,6 +192,7 @@ __device__ unsigned long long warp_select_topk(unsigned long long* buf, int n, i
     kmin = v < kmin ? v : kmin;
   }
   __syncwarp();
+  SEL_T(3);
   return kmin;
 }
 
@@ -188,6 +211,7 @@ struct __align__(16) IndexerSmemMisc {
   int abort_flag;
   alignas(16) float w[kQRows];
   uint32_t hist[kEpiWarps][256];
+  unsigned long long xch[4][16];  // per-slice exchange words of the cooperative select
 };
 
 __host__ __device__ inline int indexer_stages(int D) { return D <= 64 ? 4 : 2; }
@@ -212,6 +236,143 @@ __device__ __forceinline__ float sum2(unsigned long long v) {
   return x + y;
 }
 
+// Cooperative exact top-k select by the 4 warps (128 threads) of one epilogue
+// slice, used when the candidate buffer fits in registers (n <= 128 * E).
+// One coalesced read of the buffer into registers, radix passes (8-bit
+// digits over the 64-bit key, starting below the keys' common prefix) with
+// per-warp shared histograms, and an in-place compaction from registers.
+// hist4: the slice's 4 warp histograms (4 x 256 words); xch: 16 words of
+// exchange space; bar: the slice's named barrier id.  Returns the smallest
+// kept key.  All 128 threads must call it with the same arguments.
+template <int E>
+__device__ unsigned long long slice_select_topk(unsigned long long* buf, int n, int ksel, uint32_t* hist4,
+                                                unsigned long long* xch, int wi, uint32_t bar) {
+  const uint32_t lane = lane_id();
+  const int tid = wi * 32 + (int)lane;
+  unsigned long long k[E];
+  unsigned long long a = ~0ull, o = 0ull;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 128 + tid;
+    k[e] = i < n ? buf[i] : 0ull;
+    if (i < n) {
+      a &= k[e];
+      o |= k[e];
+    }
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    a &= shfl_xor_u64(a, m);
+    o |= shfl_xor_u64(o, m);
+  }
+  if (lane == 0) {
+    xch[wi] = a;
+    xch[4 + wi] = o;
+  }
+  named_bar(bar, 128);
+  a = xch[0] & xch[1] & xch[2] & xch[3];
+  o = xch[4] | xch[5] | xch[6] | xch[7];
+  const unsigned long long diff = a ^ o;
+  const int hb = 63 - __clzll((long long)diff);
+  unsigned long long mask = (hb == 63) ? 0ull : ~((2ull << hb) - 1ull);
+  unsigned long long prefix = a & mask;
+  int need = ksel;
+  int shift = hb >= 7 ? hb - 7 : 0;
+  uint32_t* myh = hist4 + wi * 256;
+  while (true) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) myh[lane * 8 + j] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = e * 128 + tid;
+      if (i < n && (k[e] & mask) == prefix) atomicAdd(&myh[(uint32_t)(k[e] >> shift) & 255u], 1u);
+    }
+    named_bar(bar, 128);  // histograms complete (and the previous round's xch reads done)
+    if (wi == 0) {
+      uint32_t c[8];
+      uint32_t local = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = lane * 8 + j;
+        c[j] = hist4[d] + hist4[256 + d] + hist4[512 + d] + hist4[768 + d];
+        local += c[j];
+      }
+      uint32_t suf = local;
+#pragma unroll
+      for (int m = 1; m < 32; m <<= 1) {
+        const uint32_t v = __shfl_down_sync(0xffffffffu, suf, m);
+        if (lane + m < 32) suf += v;
+      }
+      const uint32_t above_lane = suf - local;
+      const bool mine = above_lane < (uint32_t)need && (uint32_t)need <= suf;
+      if (mine) {
+        uint32_t above = above_lane;
+#pragma unroll
+        for (int j = 7; j >= 0; --j) {
+          if (above + c[j] >= (uint32_t)need) {
+            xch[8] = (unsigned long long)(lane * 8 + j);
+            xch[9] = above;
+            xch[10] = c[j];
+            break;
+          }
+          above += c[j];
+        }
+      }
+    }
+    named_bar(bar, 128);  // digit published
+    const int digit = (int)xch[8];
+    const int above = (int)xch[9];
+    const int eq = (int)xch[10];
+    need -= above;
+    prefix |= (unsigned long long)digit << shift;
+    mask |= 0xFFull << shift;
+    if (eq == need || shift == 0) break;
+    shift = shift >= 8 ? shift - 8 : 0;
+  }
+  // compaction: keys >= prefix are exactly the top ksel
+  const unsigned long long theta = prefix;
+  int cnt = 0;
+  unsigned long long kmin = ~0ull;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 128 + tid;
+    if (i < n && k[e] >= theta) {
+      ++cnt;
+      kmin = k[e] < kmin ? k[e] : kmin;
+    }
+  }
+  int incl = cnt;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, m);
+    if ((int)lane >= m) incl += v;
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const unsigned long long v = shfl_xor_u64(kmin, m);
+    kmin = v < kmin ? v : kmin;
+  }
+  named_bar(bar, 128);  // everyone has read xch[8..10]
+  if (lane == 31) xch[wi] = (unsigned long long)incl;
+  if (lane == 0) xch[4 + wi] = kmin;
+  named_bar(bar, 128);
+  int base = 0;
+  for (int w = 0; w < wi; ++w) base += (int)xch[w];
+  int pos = base + incl - cnt;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 128 + tid;
+    if (i < n && k[e] >= theta) buf[pos++] = k[e];
+  }
+  unsigned long long m0 = xch[4], m1 = xch[5], m2 = xch[6], m3 = xch[7];
+  kmin = m0 < m1 ? m0 : m1;
+  kmin = m2 < kmin ? m2 : kmin;
+  kmin = m3 < kmin ? m3 : kmin;
+  named_bar(bar, 128);  // compaction stores done, xch free
+  return kmin;
+}
+
 // ------------------------------------------------------------------ epilogue
 // Warps 2..9.  Per (key tile, group): TMEM -> fp32 scores (ReLU, w, sum over
 // heads in-thread), release the accumulator, then feed the streaming top-k.
@@ -220,18 +381,35 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
                                                  int warp, uint32_t lane, int nrounds, int nblocks, int grid) {
   constexpr int QC = kQRows / H;
   constexpr int QG = kGroupCols / H;
-  constexpr int NQH = (kGroupCols / 2) / H;
+  constexpr int NQH = EpiCfg<H>::NQW;      // queries per epilogue warp
+  constexpr int CW = EpiCfg<H>::CW;        // columns per epilogue warp
+  constexpr int NW = EpiCfg<H>::WARPS;
   const int e = warp - 2;
   const int qd = warp & 3;  // TMEM lane quadrant this warp may access
-  const int hf = e >> 2;    // column half of each group
+  const int hf = e >> 2;    // column slice of each group
   const int etid = e * 32 + (int)lane;
   const uint32_t lt = (1u << lane) - 1u;
   volatile int* abort_flag = &ms->abort_flag;
   volatile int* vcnt = ms->cnt;
   volatile unsigned long long* vthr = ms->thr;
   uint32_t* hist = ms->hist[e];
+  uint32_t* hist4 = ms->hist[4 * hf];       // the slice's four warp histograms
+  unsigned long long* xch = ms->xch[hf];
+  // exact top-ksel of query j's buffer (n > ksel keys), compacted in place;
+  // returns the new threshold.  Called uniformly by the slice's 4 warps.
+  auto select = [&](int jj, unsigned long long* buf, int n) -> unsigned long long {
+    if (n <= 128 * kSelRegs) return slice_select_topk<kSelRegs>(buf, n, p.ksel, hist4, xch, qd, 1 + hf);
+    unsigned long long th = 0ull;
+    if ((jj & 3) == qd) th = warp_select_topk(buf, n, p.ksel, hist);
+    if (lane == 0 && (jj & 3) == qd) xch[15] = th;
+    named_bar(1 + hf, 128);
+    th = xch[15];
+    named_bar(1 + hf, 128);
+    return th;
+  };
   unsigned long long* cand_cta = p.cand + (size_t)blockIdx.x * QC * p.cap;
   uint32_t aph[2] = {0, 0};
+  unsigned long long thr_reg[2][NQH];  // per group: this warp's cached thresholds (change only at sync points)
 
   for (int r = 0; r < nrounds; ++r) {
     const int i = block_index(r, blockIdx.x, grid);
@@ -241,8 +419,8 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
     const int s0 = blk * QC;
     const int ntiles = (MODE == kModeTopk) ? block_key_tiles(p, QC, blk) : ceil_div(p.T, kKeysPerTile);
 
-    named_bar(3, 32 * kEpiWarps);  // the previous block is done with w / lim / thr / cnt
-    for (int x = etid; x < QC * H; x += 32 * kEpiWarps) {
+    named_bar(7, 32 * NW);  // the previous block is done with w / lim / thr / cnt
+    for (int x = etid; x < QC * H; x += 32 * NW) {
       const int s = s0 + x / H;
       float wv = 0.f;
       if (s < p.S) {
@@ -257,45 +435,59 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
       ms->thr[etid] = 0ull;
       ms->cnt[etid] = 0;
     }
-    named_bar(3, 32 * kEpiWarps);
+    named_bar(7, 32 * NW);
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+#pragma unroll
+      for (int jj = 0; jj < NQH; ++jj) thr_reg[g][jj] = 0ull;
 
     bool ok = true;
     for (int t = 0; t < ntiles && ok; ++t) {
       const int tkey = t * kKeysPerTile + qd * 32 + (int)lane;
       for (int g = 0; g < 2; ++g) {
+        if (warp == 2 && lane == 0) SI_ITRACE(2, r, t, 4 * g + 0);
         if (!mbar_wait(&ms->acc_full[g], aph[g], abort_flag, p.status, kErrWaitAccFull)) {
           ok = false;
           break;
         }
+        if (warp == 2 && lane == 0) SI_ITRACE(2, r, t, 4 * g + 1);
         aph[g] ^= 1;
         tc_fence_after();
         // acc2[jj] holds two partial sums (even / odd heads) updated with the
         // packed fp32 FMA (fma.rn.f32x2): ReLU is one fmax per element, the
         // weight multiply-add half an instruction per element.
-        unsigned long long acc2[NQH];
+        // Four independent packed accumulators per query (by head index mod 8)
+        // keep the FMA dependency chains short.
+        unsigned long long acc2[NQH][4];
 #pragma unroll
-        for (int jj = 0; jj < NQH; ++jj) acc2[jj] = 0ull;
-        const uint32_t tbase = tmem + ((uint32_t)(qd * 32) << 16) + g * kGroupCols + hf * (kGroupCols / 2);
-        const float* wrow = ms->w + g * kGroupCols + hf * (kGroupCols / 2);
+        for (int jj = 0; jj < NQH; ++jj)
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+          for (int u = 0; u < 4; ++u) acc2[jj][u] = 0ull;
+        const uint32_t tbase = tmem + ((uint32_t)(qd * 32) << 16) + g * kGroupCols + hf * CW;
+        const float* wrow = ms->w + g * kGroupCols + hf * CW;
+#pragma unroll
+        for (int c = 0; c < CW / 64; ++c) {
           float v0[32], v1[32];
           tmem_ld32x2_sync(tbase + c * 64, tbase + c * 64 + 32, v0, v1);
 #pragma unroll
-          for (int h2 = 0; h2 < 16; ++h2) {
-            const int ca = c * 64 + h2 * 2, cb = c * 64 + 32 + h2 * 2;
-            const unsigned long long wa = reinterpret_cast<const unsigned long long*>(wrow + c * 64)[h2];
-            const unsigned long long wb = reinterpret_cast<const unsigned long long*>(wrow + c * 64 + 32)[h2];
-            ffma2(acc2[ca / H], relu2(v0[h2 * 2], v0[h2 * 2 + 1]), wa);
-            ffma2(acc2[cb / H], relu2(v1[h2 * 2], v1[h2 * 2 + 1]), wb);
+          for (int h4 = 0; h4 < 8; ++h4) {
+            const ulonglong2 wa = reinterpret_cast<const ulonglong2*>(wrow + c * 64)[h4];
+            const ulonglong2 wb = reinterpret_cast<const ulonglong2*>(wrow + c * 64 + 32)[h4];
+            const int ca = c * 64 + h4 * 4, cb = c * 64 + 32 + h4 * 4;
+            ffma2(acc2[ca / H][(h4 & 1) * 2 + 0], relu2(v0[h4 * 4 + 0], v0[h4 * 4 + 1]), wa.x);
+            ffma2(acc2[ca / H][(h4 & 1) * 2 + 1], relu2(v0[h4 * 4 + 2], v0[h4 * 4 + 3]), wa.y);
+            ffma2(acc2[cb / H][(h4 & 1) * 2 + 0], relu2(v1[h4 * 4 + 0], v1[h4 * 4 + 1]), wb.x);
+            ffma2(acc2[cb / H][(h4 & 1) * 2 + 1], relu2(v1[h4 * 4 + 2], v1[h4 * 4 + 3]), wb.y);
           }
         }
         float acc[NQH];
 #pragma unroll
-        for (int jj = 0; jj < NQH; ++jj) acc[jj] = sum2(acc2[jj]);
+        for (int jj = 0; jj < NQH; ++jj)
+          acc[jj] = (sum2(acc2[jj][0]) + sum2(acc2[jj][1])) + (sum2(acc2[jj][2]) + sum2(acc2[jj][3]));
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ms->acc_empty[g]);
+        if (warp == 2 && lane == 0) SI_ITRACE(2, r, t, 4 * g + 2);
 
         if (MODE == kModeScore) {
 #pragma unroll
@@ -306,24 +498,33 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
           continue;
         }
 
-        // ---- streaming top-k: make room, then insert this tile's candidates
-        named_bar(1 + hf, 128);
-        bool any = false;
+        // ---- streaming top-k.  Every kSyncTiles tiles the half's four warps
+        // meet: a query whose buffer could not absorb kSyncTiles more tiles of
+        // inserts is flushed by its owner warp, and thresholds are re-read.
+        // In between, inserts only need the cached threshold and an atomic.
+        if (t % kSyncTiles == 0) {
+          named_bar(1 + hf, 128);
+          const int room = p.cap - kSyncTiles * kKeysPerTile;
+          bool any = false;
 #pragma unroll
-        for (int jj = 0; jj < NQH; ++jj) any |= vcnt[g * QG + hf * NQH + jj] > p.cap - kKeysPerTile;
-        if (any) {
+          for (int jj = 0; jj < NQH; ++jj) any |= vcnt[g * QG + hf * NQH + jj] > room;
+          if (any) {
 #pragma unroll
-          for (int jj = 0; jj < NQH; ++jj) {
-            const int j = g * QG + hf * NQH + jj;
-            if ((jj & 3) == qd && vcnt[j] > p.cap - kKeysPerTile) {
-              const unsigned long long th = warp_select_topk(cand_cta + (size_t)j * p.cap, vcnt[j], p.ksel, hist);
-              if (lane == 0) {
-                vthr[j] = th;
-                vcnt[j] = p.ksel;
+            for (int jj = 0; jj < NQH; ++jj) {
+              const int j = g * QG + hf * NQH + jj;
+              const int n = vcnt[j];
+              if (n > room) {
+                const unsigned long long th = select(jj, cand_cta + (size_t)j * p.cap, n);
+                if (qd == 0 && lane == 0) {
+                  vthr[j] = th;
+                  vcnt[j] = p.ksel;
+                }
               }
             }
+            named_bar(1 + hf, 128);
           }
-          named_bar(1 + hf, 128);
+#pragma unroll
+          for (int jj = 0; jj < NQH; ++jj) thr_reg[g][jj] = vthr[g * QG + hf * NQH + jj];
         }
 #pragma unroll
         for (int jj = 0; jj < NQH; ++jj) {
@@ -332,7 +533,7 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
           if (MODE == kModeTopkMask && legal)
             legal = p.mask[((size_t)b * p.S + (s0 + j)) * p.T + tkey] != 0;
           const unsigned long long key = make_key(acc[jj], tkey);
-          const bool pass = legal && key > vthr[j];
+          const bool pass = legal && key > thr_reg[g][jj];
           const uint32_t bal = __ballot_sync(0xffffffffu, pass);
           if (bal) {
             const int leader = __ffs(bal) - 1;
@@ -342,6 +543,7 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
             if (pass) cand_cta[(size_t)j * p.cap + base + __popc(bal & lt)] = key;
           }
         }
+        if (warp == 2 && lane == 0) SI_ITRACE(2, r, t, 4 * g + 3);
       }
     }
     if (!ok) break;
@@ -355,15 +557,16 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
         for (int jj = 0; jj < NQH; ++jj) {
           const int j = g * QG + hf * NQH + jj;
           const int s = s0 + j;
-          if ((jj & 3) != qd || s >= p.S) continue;
+          if (s >= p.S) continue;  // uniform across the slice
           unsigned long long* buf = cand_cta + (size_t)j * p.cap;
           int n = vcnt[j];
           if (n > p.ksel) {
-            warp_select_topk(buf, n, p.ksel, hist);
+            select(jj, buf, n);
             n = p.ksel;
           }
           unsigned long long* dst = p.out_keys + ((size_t)b * p.S + s) * p.ksel;
-          for (int x = (int)lane; x < p.ksel; x += 32) dst[x] = x < n ? buf[x] : 0ull;
+          const int tid = qd * 32 + (int)lane;
+          for (int x = tid; x < p.ksel; x += 128) dst[x] = x < n ? buf[x] : 0ull;
         }
       }
     }
@@ -371,13 +574,12 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
 }
 
 template <int H, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(EpiCfg<H>::THREADS, 1)
     indexer_topk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         IndexerParams p, uint32_t idesc) {
   constexpr int QC = kQRows / H;         // queries per block
   constexpr int QG = kGroupCols / H;     // queries per group
-  constexpr int NQH = (kGroupCols / 2) / H;  // queries per half-group (per epilogue warp)
-  static_assert(NQH >= 1 && QC <= kMaxQC, "unsupported head count");
+  static_assert(EpiCfg<H>::NQW >= 1 && QC <= kMaxQC, "unsupported head count");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -401,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int g = 0; g < 2; ++g) {
       mbar_init(&ms->acc_full[g], 1);
-      mbar_init(&ms->acc_empty[g], kEpiWarps);
+      mbar_init(&ms->acc_empty[g], EpiCfg<H>::WARPS);
     }
     mbar_init(&ms->q_full, 1);
     mbar_init(&ms->q_empty, 1);
@@ -445,10 +647,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int krow = b * p.T;
         bool ok = true;
         for (int t = 0; t < ntiles; ++t) {
+          SI_ITRACE(0, r, t, 0);
           if (!mbar_wait(&ms->k_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
             ok = false;
             break;
           }
+          SI_ITRACE(0, r, t, 1);
           mbar_expect_tx(&ms->k_full[st], kbytes);
           uint8_t* dst = sK + (size_t)st * NA * kKeysPerTile * 128;
           for (int a = 0; a < NA; ++a)
@@ -479,10 +683,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         bool ok = true;
         for (int t = 0; t < ntiles && ok; ++t) {
+          SI_ITRACE(1, r, t, 0);
           if (!mbar_wait(&ms->k_full[st], kph, abort_flag, p.status, kErrWaitTmaFull)) {
             ok = false;
             break;
           }
+          SI_ITRACE(1, r, t, 1);
           tc_fence_after();
           const uint32_t kbase = smem_u32(sK + (size_t)st * NA * kKeysPerTile * 128);
           for (int g = 0; g < 2; ++g) {
@@ -491,6 +697,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             aph[g] ^= 1;
+            SI_ITRACE(1, r, t, 2 + g);
             tc_fence_after();
             const uint32_t qbase = smem_u32(sQ) + g * kGroupCols * 128;
             const uint32_t d_tmem = tmem + g * kGroupCols;
@@ -601,7 +808,7 @@ __global__ void __launch_bounds__(256) topk_row_sort_kernel(unsigned long long* 
 
 namespace si {
 
-static int pick_cap(int ksel) { return ((2 * ksel + kKeysPerTile + 31) / 32) * 32; }
+static int pick_cap(int ksel) { return ((2 * ksel + kSyncTiles * kKeysPerTile + 31) / 32) * 32; }
 
 static int indexer_grid(int nblocks) {
   const int sms = device_sm_count();
@@ -626,7 +833,7 @@ static cudaError_t launch_indexer_t(const CUtensorMap& mq, const CUtensorMap& mk
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  indexer_topk_kernel<H, MODE><<<grid, kThreads, smem, stream>>>(mq, mk, p, idesc);
+  indexer_topk_kernel<H, MODE><<<grid, EpiCfg<H>::THREADS, smem, stream>>>(mq, mk, p, idesc);
   return cudaGetLastError();
 }
 
@@ -673,6 +880,18 @@ static int check_indexer_args(const void* q, const void* k, const void* w, int B
   return 0;
 }
 
+#ifdef SI_IDX_TRACE
+static unsigned long long* g_idx_trace = nullptr;
+}  // namespace si
+extern "C" SI_API void si_debug_set_idx_trace(unsigned long long* t) { si::g_idx_trace = t; }
+extern "C" SI_API void si_debug_set_sel_trace(unsigned long long* t) {
+  cudaMemcpyToSymbol(si::g_sel_trace, &t, sizeof(t));
+  unsigned int z = 0;
+  cudaMemcpyToSymbol(si::g_sel_count, &z, sizeof(z));
+}
+namespace si {
+#endif
+
 static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
                        int H, int D, int ksel, int ratio, const uint8_t* mask, int mode, int64_t* out_idx,
                        float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream, long long s_offset = 0,
@@ -713,6 +932,9 @@ static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf1
   const int QC = kQRows / H;
   p.nblk_per_batch = ceil_div(S, QC);
   p.s_offset = s_offset;
+#ifdef SI_IDX_TRACE
+  p.trace = g_idx_trace;
+#endif
   const int grid = indexer_grid(B * p.nblk_per_batch);
   const uint32_t idesc = umma_idesc_f16(kKeysPerTile, kGroupCols, ab_fp16 ? 0 : 1);
   cudaError_t e;

@@ -43,9 +43,24 @@ namespace si {
 constexpr int kKeysPerTile = 128;   // UMMA M
 constexpr int kGroupCols = 256;     // UMMA N per group
 constexpr int kQRows = 512;         // (query, head) rows resident per block
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kEpiWarps = 16;      // maximum epilogue warps (hist scratch sizing)
+
+// Epilogue shape per head count: NS column slices of each 256-column group,
+// one warp per (TMEM lane quadrant, slice).  H_I <= 64 uses 16 warps (four per
+// SM sub-partition, one 64-column slice = one H_I=64 query each) so the
+// epilogue hides TMEM / shared-memory latency; H_I = 128 uses 8 warps with
+// 128-column slices so a query never straddles two warps.
+template <int H>
+struct EpiCfg {
+  static constexpr int NS = (H == 128) ? 2 : 4;
+  static constexpr int CW = kGroupCols / NS;   // columns per warp
+  static constexpr int NQW = CW / H;           // queries per warp
+  static constexpr int WARPS = 4 * NS;
+  static constexpr int THREADS = 32 * (2 + WARPS);
+};
 constexpr int kMaxQC = 32;          // H >= 16
+constexpr int kSyncTiles = 4;
+constexpr int kSelRegs = 12;        // keys per thread held in registers by the cooperative select       // top-k capacity checks / flushes every kSyncTiles key tiles
 
 enum IndexerMode : int { kModeTopk = 0, kModeTopkMask = 1, kModeScore = 2 };
 
@@ -63,7 +78,21 @@ struct IndexerParams {
   int* status;                // device status word
   int nblk_per_batch;         // ceil(S / QC)
   long long s_offset;         // global position of local query 0 (causal mask uses s_offset + s)
+  unsigned long long* trace;  // debug builds (SI_IDX_TRACE) only
 };
+
+#ifdef SI_IDX_TRACE
+// [role 0..2][tile < 512][point < 8], first block of CTA 0 only
+#define SI_ITRACE(role, r, tile, pt)                                                        \
+  do {                                                                                      \
+    if (p.trace && blockIdx.x == 0 && (r) == 0 && (tile) < 512)                             \
+      p.trace[((role) * 512 + (tile)) * 8 + (pt)] = globaltimer();                          \
+  } while (0)
+#else
+#define SI_ITRACE(role, r, tile, pt) \
+  do {                               \
+  } while (0)
+#endif
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
