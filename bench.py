@@ -62,7 +62,9 @@ def parse():
 
 def config(a, world):
     return {
-        "workload": f"V4-Flash indexer+top-k S={a.S} (configs[1])",
+        "workload": (f"V4-Flash indexer+top-k S={a.S} (configs[1])" if (a.H, a.k) == (64, 512)
+                     else f"V4-Pro-dimension indexer+top-k S={a.S} H_I={a.H} top_k={a.k} (configs[2])"
+                     if (a.H, a.k) == (128, 1024) else f"indexer+top-k S={a.S} H_I={a.H} top_k={a.k}"),
         "B": 1, "S": a.S, "H_I": a.H, "D_I": a.D, "T": a.S // a.ratio, "top_k": a.k, "causal_ratio": a.ratio,
         "chunk_s_chunk_t": "2048x8192 semantics (result is chunk-independent)",
         "parallelism": f"S-shard x{world}" if world > 1 else "single GPU",

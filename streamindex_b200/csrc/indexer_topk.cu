@@ -398,7 +398,8 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
   // exact top-ksel of query j's buffer (n > ksel keys), compacted in place;
   // returns the new threshold.  Called uniformly by the slice's 4 warps.
   auto select = [&](int jj, unsigned long long* buf, int n) -> unsigned long long {
-    if (n <= 128 * kSelRegs) return slice_select_topk<kSelRegs>(buf, n, p.ksel, hist4, xch, qd, 1 + hf);
+    constexpr int SR = (H == 128) ? 20 : kSelRegs;  // H_I = 128 runs 8 epilogue warps with a larger register budget
+    if (n <= 128 * SR) return slice_select_topk<SR>(buf, n, p.ksel, hist4, xch, qd, 1 + hf);
     unsigned long long th = 0ull;
     if ((jj & 3) == qd) th = warp_select_topk(buf, n, p.ksel, hist);
     if (lane == 0 && (jj & 3) == qd) xch[15] = th;

@@ -75,3 +75,9 @@ def test_indexer_score_materialised():
     ref = oracle.lightning_indexer(q, kk, w)
     assert oracle.score_close(got, ref, 1e-2)
     assert oracle.norm_corr(got, ref) < 5e-3
+
+
+def test_indexer_topk_v4_pro_dims():
+    """BASELINE config 3 dims at small S: H_I=128, top_k=1024, ratio 4."""
+    gi, gv, oi, ov = _run(1, 8192, 128, 128, 2048, 1024, ratio=4, seed=2)
+    _assert_parity(gi, gv, oi, ov)
