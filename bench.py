@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-queries", type=int, default=96)
     ap.add_argument("--no-gather", action="store_true")
-    ap.add_argument("--workload", default="indexer", choices=["indexer", "attn"],
+    ap.add_argument("--workload", default="indexer", choices=["indexer", "attn", "csa"],
                     help="indexer: the headline metric (default); attn: BASELINE configs[3] sparse attention")
     return ap.parse_args()
 
@@ -496,8 +496,60 @@ def run_attn(a):
     print(json.dumps(line), flush=True)
 
 
+def run_csa(a):
+    """CSA layer forward, B=2, S=131072, H=64, D=576/512, H_I=64, D_I=128, m=4, k=512, n_win=128.
+
+    One step = mean-pool compressor (kv and indexer keys) -> fused indexer + top-k
+    -> index build -> sparse attention, through flash_csa_forward."""
+    from streamindex_b200.csa import flash_csa_forward, mean_pool_compress
+
+    B, S, H, D, DV, HI, DI, m, k, nwin = 2, a.S, 64, 576, 512, 64, 128, 4, 512, 128
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    x_kv = torch.randn((B, S, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    x_k = torch.randn((B, S, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
+    q = torch.randn((B, S, H, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    q_idx = torch.randn((B, S, HI, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
+    w = torch.randn((B, S, HI), generator=g, device=dev, dtype=torch.float32)
+    sink = torch.zeros(H, dtype=torch.float32, device=dev)
+
+    def step():
+        kvc = mean_pool_compress(x_kv, m)
+        kc = mean_pool_compress(x_k, m)
+        return flash_csa_forward(q, x_kv, kvc, q_idx, kc, w, sink, n_win=nwin, top_k=k, m=m, d_v=DV)
+
+    for _ in range(a.warmup):
+        step()
+    clocks = ClockSampler(0)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / a.steps
+    line = {
+        "metric": "CSA layer forward (BASELINE configs[4]) Mqueries/s", "value": B * S / (ms * 1e-3) / 1e6,
+        "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"flash_csa_forward B=2 S={S} H=64 D=576/512 H_I=64 D_I=128 m=4 top_k=512 n_win=128",
+                   "path": "mean-pool x2 -> fused indexer+top-k -> index build -> split-kv sparse attention"},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
+    if a.workload == "csa":
+        if a.S == 1 << 20:
+            a.S = 131072
+        run_csa(a)
+        return
     if a.workload == "attn":
         if a.S == 1 << 20:
             a.S = 65536
