@@ -29,6 +29,7 @@
 // Warp roles (192 threads): warp 0 TMA (Q + gathers), warp 1 TMEM alloc +
 // UMMA issue, warps 2-5 softmax / correction / output.
 #include <cuda_bf16.h>
+#include <cstdlib>
 
 #include "capi_common.h"
 #include "ptx.cuh"
@@ -38,7 +39,7 @@ namespace si {
 namespace attn {
 
 constexpr int kHeads = 64;    // UMMA M (heads per work item)
-constexpr int kThreads = 448;
+constexpr int kThreads = 480;   // + warp 14: TMA row gathers
 constexpr int kGatherWarps = 8;   // warps 6-13
 constexpr int kSmemMax = 232448;
 
@@ -59,6 +60,7 @@ struct Params {
   float* lse;          // [B,S,H] or null
   int* status;
   int hgroups;         // ceil(H/64)
+  int na_tma;          // leading atoms of each kv row gathered by TMA (warp 14); the rest by cp.async
   unsigned long long* trace;  // debug builds (SI_ATTN_TRACE) only: per-role timestamps of CTA 0
 };
 
@@ -317,7 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NST; ++i) {
-      mbar_init(&ms->kv_full[i], kGatherWarps * 32);  // one cp.async completion arrival per gather thread
+      // one cp.async completion arrival per gather thread (+ the TMA warp's expect_tx arrival)
+      mbar_init(&ms->kv_full[i], kGatherWarps * 32 + (p.na_tma > 0 ? 1 : 0));
       mbar_init(&ms->kv_empty[i], 1);
     }
     mbar_init(&ms->q_full, 1);
@@ -361,6 +364,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     }
+  } else if (warp == 6 + kGatherWarps) {
+    // ------------------------------------------------------------ TMA row gathers (gather4) of atoms [0, na_tma)
+    if (p.na_tma > 0) {
+      uint32_t st = 0, kph = 0;
+      const int g4 = (int)lane & 7;
+      const int a = (int)lane >> 3;
+      for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
+        const int bs = it / p.hgroups;
+        const int b = bs / p.S, s = bs % p.S;
+        bool valid_next;
+        int row_next = gather_row(p, b, s, (int)lane, valid_next);
+        bool ok = true;
+        for (int t = 0; t < ntiles; ++t) {
+          const int row = valid_next ? b * p.Nkv + row_next : p.B * p.Nkv;  // out of range: zero fill
+          if (t + 1 < ntiles) row_next = gather_row(p, b, s, (t + 1) * NK + (int)lane, valid_next);
+          if (!mbar_wait(&ms->kv_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) mbar_expect_tx(&ms->kv_full[st], (uint32_t)(p.na_tma * NK * 128));
+          __syncwarp();
+          const int r0 = __shfl_sync(0xffffffffu, row, 4 * g4 + 0);
+          const int r1 = __shfl_sync(0xffffffffu, row, 4 * g4 + 1);
+          const int r2 = __shfl_sync(0xffffffffu, row, 4 * g4 + 2);
+          const int r3 = __shfl_sync(0xffffffffu, row, 4 * g4 + 3);
+          if (a < p.na_tma)
+            tma_gather4(sKV + (size_t)st * SB + a * NK * 128 + g4 * 4 * 128, &map_kv, &ms->kv_full[st], a * 64, r0,
+                        r1, r2, r3);
+          __syncwarp();
+          if (++st == (uint32_t)NST) {
+            st = 0;
+            kph ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+    }
   } else if (warp >= 6) {
     // ------------------------------------------------------------ KV row gathers (cp.async)
     // A tile is NK rows x NA 128-byte atoms.  One warp instruction copies 4
@@ -390,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (tr) SI_TRACE(0, ii, t, 1);
         const uint32_t base = smem_u32(sKV + (size_t)st * SB);
-        for (int q = gw; q < NA * 8; q += kGatherWarps) {
+        for (int q = p.na_tma * 8 + gw; q < NA * 8; q += kGatherWarps) {
           const int u = q * 4 + (int)(lane >> 3);
           const int r = u & (NK - 1);
           const int a = u / NK;
@@ -580,6 +620,9 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
   p.idx = topk_idxs;
   p.kv = reinterpret_cast<const __nv_bfloat16*>(kv);
   p.kv2 = reinterpret_cast<const __nv_bfloat16*>(kv2);
+  // two atoms per row go through TMA gathers when kv is one tensor (measured best at D=576)
+  p.na_tma = Nkv2 > 0 ? 0 : (NA >= 6 ? 2 : 0);
+  if (const char* e = getenv("SI_ATTN_NA_TMA")) p.na_tma = atoi(e) < NA ? atoi(e) : NA;
   p.Nkv1 = Nkv1;
   p.sink = attn_sink;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
