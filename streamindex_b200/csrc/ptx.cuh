@@ -10,6 +10,10 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#ifndef SI_WAIT_BACKOFF_NS
+#define SI_WAIT_BACKOFF_NS 64
+#endif
+
 #ifndef SI_WAIT_NS
 #define SI_WAIT_NS 4000000000ull  // 4 s
 #endif
@@ -87,21 +91,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended in hardware (up to ~hint ns, woken early when the phase completes)
+// instead of spinning, so waiting warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(200000u)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait.  Returns false (after recording `code`) on timeout or when
 // another role of the CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > SI_WAIT_NS) {
-        atomicCAS(status, 0, code);
-        *abort_flag = 1;
-        return false;
-      }
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    __nanosleep(SI_WAIT_BACKOFF_NS);  // poll sparsely: waiting warps yield their issue slots
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > SI_WAIT_NS) {
+      atomicCAS(status, 0, code);
+      *abort_flag = 1;
+      return false;
     }
   }
 }

@@ -29,7 +29,6 @@
 // Warp roles (192 threads): warp 0 TMA (Q + gathers), warp 1 TMEM alloc +
 // UMMA issue, warps 2-5 softmax / correction / output.
 #include <cuda_bf16.h>
-#include <cstdlib>
 
 #include "capi_common.h"
 #include "ptx.cuh"
@@ -622,7 +621,6 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
   p.kv2 = reinterpret_cast<const __nv_bfloat16*>(kv2);
   // two atoms per row go through TMA gathers when kv is one tensor (measured best at D=576)
   p.na_tma = Nkv2 > 0 ? 0 : (NA >= 6 ? 2 : 0);
-  if (const char* e = getenv("SI_ATTN_NA_TMA")) p.na_tma = atoi(e) < NA ? atoi(e) : NA;
   p.Nkv1 = Nkv1;
   p.sink = attn_sink;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
