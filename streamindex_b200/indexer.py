@@ -180,3 +180,72 @@ class IndexerTopk:
 
     def status(self) -> int:
         return _lib.read_status(self.ws, self.device)
+
+    def run_host(self, q_host, k_host, w_host, idx_host, scores_host, chunks: int = 8):
+        """Indexer + top-k from pinned HOST buffers into pinned HOST outputs.
+
+        The query range is cut into ``chunks`` slices.  Keys are copied once;
+        then slice c+1's q / w host-to-device copies and slice c-1's results
+        device-to-host copies run on two copy streams while slice c computes
+        (each slice is one C-ABI call with its ``s_offset``), so the PCIe
+        transfers hide behind the kernel.  Requires B == 1.  Returns once the
+        outputs are in host memory.
+        """
+        assert self.B == 1
+        for t in (q_host, k_host, w_host, idx_host, scores_host):
+            assert not t.is_cuda and t.is_pinned() and t.is_contiguous(), "host buffers must be pinned and contiguous"
+        dev = self.device
+        S, H, D, T, k = self.S, self.H, self.D, self.T, self.k
+        bounds = [S * c // chunks for c in range(chunks + 1)]
+        bounds = [min(S, ((b + 127) // 128) * 128) for b in bounds[:-1]] + [S]
+        nmax = max(b1 - b0 for b0, b1 in zip(bounds, bounds[1:]))
+        if not hasattr(self, "_hbufs") or self._hbufs[0][0].shape[1] < nmax:
+            self._hbufs = (
+                [torch.empty((1, nmax, H, D), dtype=q_host.dtype, device=dev) for _ in range(2)],
+                [torch.empty((1, nmax, H), dtype=w_host.dtype, device=dev) for _ in range(2)],
+                [torch.empty((1, nmax, k), dtype=torch.int64, device=dev) for _ in range(2)],
+                [torch.empty((1, nmax, k), dtype=torch.float32, device=dev) for _ in range(2)],
+                torch.empty((1, T, D), dtype=k_host.dtype, device=dev),
+                torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        qb, wb, ib, sb, kd, s_in, s_out = self._hbufs
+        comp = torch.cuda.current_stream(dev)
+        with torch.cuda.stream(s_in):
+            kd.copy_(k_host, non_blocking=True)
+        ev_in = [torch.cuda.Event() for _ in range(chunks)]
+        ev_done = [torch.cuda.Event() for _ in range(chunks)]
+        ev_out = [torch.cuda.Event() for _ in range(chunks)]
+
+        def load(c):
+            b0, b1 = bounds[c], bounds[c + 1]
+            slot = c & 1
+            with torch.cuda.stream(s_in):
+                if c >= 2:
+                    s_in.wait_event(ev_done[c - 2])  # slot's previous slice is no longer read
+                qb[slot][:, : b1 - b0].copy_(q_host[:, b0:b1], non_blocking=True)
+                wb[slot][:, : b1 - b0].copy_(w_host[:, b0:b1], non_blocking=True)
+                ev_in[c].record(s_in)
+
+        load(0)
+        for c in range(chunks):
+            if c + 1 < chunks:
+                load(c + 1)
+            b0, b1 = bounds[c], bounds[c + 1]
+            n = b1 - b0
+            slot = c & 1
+            comp.wait_event(ev_in[c])
+            if c >= 2:
+                comp.wait_event(ev_out[c - 2])  # the output slot has been copied out
+            if n > 0:
+                _lib.check(self.lib.si_indexer_topk_ex(
+                    qb[slot].data_ptr(), kd.data_ptr(), wb[slot].data_ptr(), self.w_bf16, self.fp16, 1, n, T, H, D,
+                    k, self.ratio, None, self.s_offset + b0, 0, ib[slot].data_ptr(), sb[slot].data_ptr(), self.ws.data_ptr(),
+                    self.ws_bytes, _lib.stream_handle(dev)))
+            ev_done[c].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done[c])
+                idx_host[:, b0:b1].copy_(ib[slot][:, :n], non_blocking=True)
+                scores_host[:, b0:b1].copy_(sb[slot][:, :n], non_blocking=True)
+                ev_out[c].record(s_out)
+        comp.wait_event(ev_out[chunks - 1])
+        comp.synchronize()
+        return idx_host, scores_host

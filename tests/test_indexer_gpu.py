@@ -81,3 +81,20 @@ def test_indexer_topk_v4_pro_dims():
     """BASELINE config 3 dims at small S: H_I=128, top_k=1024, ratio 4."""
     gi, gv, oi, ov = _run(1, 8192, 128, 128, 2048, 1024, ratio=4, seed=2)
     _assert_parity(gi, gv, oi, ov)
+
+
+def test_run_host_pipelined_matches_device_path():
+    """Host-buffer pipelined path (query slices, overlapped copies) == device path, bit for bit."""
+    from streamindex_b200.indexer import IndexerTopk
+
+    S, H, D, T, k = 3000, 64, 128, 750, 64
+    q, kk, w = oracle.indexer_inputs(1, S, H, D, T, seed=21)
+    plan = IndexerTopk(1, S, T, H, D, k, causal_ratio=4, device="cuda")
+    di, dv = plan.run(q.cuda(), kk.cuda(), w.cuda())
+    di, dv = di.cpu().clone(), dv.cpu().clone()
+    hq, hk, hw = q.pin_memory(), kk.pin_memory(), w.pin_memory()
+    hi = torch.empty((1, S, k), dtype=torch.int64).pin_memory()
+    hs = torch.empty((1, S, k), dtype=torch.float32).pin_memory()
+    for chunks in (1, 5):
+        plan.run_host(hq, hk, hw, hi, hs, chunks=chunks)
+        assert torch.equal(hi, di) and torch.equal(hs, dv)
