@@ -140,6 +140,11 @@ SI_API int si_scores_topk(const float* scores, int B, int S, int T, int top_k, i
 SI_API int si_csa_build_idx(const int64_t* comp_idx, int B, int S, int top_k, int n_win, int32_t* out,
                             cudaStream_t stream);
 
+/* HCA attention index list [B,S,n_win+n_comp] int32: sliding window, then all
+ * compressed blocks legal for the query ((i+1)*m_prime - 1 <= s) offset by S,
+ * else -1.  Replaces build_hca_topk_idxs (flash_sparse/hca.py:24-51). */
+SI_API int si_hca_build_idx(int B, int S, int n_win, int n_comp, int m_prime, int32_t* out, cudaStream_t stream);
+
 /* Mean-pool compressor [B,S,C] bf16 -> [B,S/m,C] bf16 (trailing S % m tokens
  * dropped).  Equals reference_token_compressor(overlap=False) with zero scores
  * and bias (flash_sparse/reference.py:234-240). */

@@ -28,6 +28,8 @@ from .csa import (  # noqa: F401
     build_csa_topk_idxs,
     mean_pool_compress,
     csa_forward,
+    build_hca_topk_idxs,
+    hca_forward,
 )
 from .metrics import set_recall, norm_corr, score_close  # noqa: F401
 from .inputs import indexer_inputs, attn_inputs  # noqa: F401

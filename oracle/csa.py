@@ -10,6 +10,9 @@
   (``reference.py:234-240``) with zero scores and zero bias, i.e. uniform
   softmax weights ``1/m`` over each block of ``m`` tokens; trailing
   ``S % m`` tokens dropped (``reference.py:227-231``).
+* ``build_hca_topk_idxs`` / ``hca_forward`` — ``flash_sparse/hca.py:24-51`` and
+  ``reference_hca_forward`` (``flash_sparse/reference.py:411-452``): window plus
+  every compressed block with ``(i+1)*m' - 1 <= s``.
 * ``csa_forward`` — ``flash_csa_forward`` (``flash_sparse/csa.py:86-207``)
   on the reference path: indexer -> index build -> ``cat[kv; kv_compressed]``
   -> sparse attention.
@@ -85,3 +88,21 @@ def csa_forward(
     kv_full = torch.cat([kv, kv_compressed], dim=1)
     o, lse = sparse_attn(q, kv_full, attn_sink, idxs, softmax_scale, d_v=d_v)
     return o, lse, idxs
+
+
+def build_hca_topk_idxs(B: int, S: int, n_win: int, n_compressed: int, m_prime: int) -> torch.Tensor:
+    win = sliding_window_idxs(B, S, n_win)
+    block_last = (torch.arange(n_compressed) + 1) * m_prime - 1
+    legal = torch.arange(S).unsqueeze(-1) >= block_last
+    base = torch.arange(n_compressed).view(1, 1, -1).expand(B, S, -1)
+    comp = torch.where(legal.unsqueeze(0).expand(B, -1, -1), base, torch.full_like(base, -1))
+    return torch.cat([win.long(), compressed_to_global(comp, S).long()], dim=-1).int()
+
+
+def hca_forward(q, kv, kv_compressed, attn_sink, n_win: int, m_prime: int, softmax_scale=None, d_v=None):
+    """Reference HCA forward.  Returns ``(o fp32, lse, idx int32)``."""
+    B, S, H, D = q.shape
+    idx = build_hca_topk_idxs(B, S, n_win, kv_compressed.shape[1], m_prime)
+    kv_full = torch.cat([kv, kv_compressed], dim=1)
+    o, lse = sparse_attn(q, kv_full, attn_sink, idx, softmax_scale, d_v=d_v)
+    return o, lse, idx

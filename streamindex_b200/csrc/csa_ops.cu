@@ -92,3 +92,44 @@ int si_mean_pool(const void* x, int B, int S, int C, int m, void* out, cudaStrea
 }
 
 }  // extern "C"
+
+namespace si {
+
+// HCA index list [B,S,n_win+n_comp]: the sliding window, then every compressed
+// block i legal for query s ((i+1)*m' - 1 <= s), offset by S, else -1
+// (flash_sparse/hca.py:24-51).
+__global__ void hca_build_idx_kernel(int B, int S, int n_win, int n_comp, int m_prime, int32_t* __restrict__ out) {
+  const int W = n_win + n_comp;
+  const long long total = (long long)B * S * W;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int col = (int)(i % W);
+    const int s = (int)((i / W) % S);
+    int v;
+    if (col < n_win) {
+      const int pos = s - n_win + 1 + col;
+      v = (pos >= 0 && pos <= s) ? pos : -1;
+    } else {
+      const int c = col - n_win;
+      v = ((long long)(c + 1) * m_prime - 1 <= s) ? c + S : -1;
+    }
+    out[i] = v;
+  }
+}
+
+}  // namespace si
+
+extern "C" {
+
+int si_hca_build_idx(int B, int S, int n_win, int n_comp, int m_prime, int32_t* out, cudaStream_t stream) {
+  if (B < 1 || S < 0 || n_win < 0 || n_comp < 0 || m_prime < 1) return si::fail("hca_build_idx: bad sizes");
+  if ((long long)S + n_comp >= (1ll << 31)) return si::fail("hca_build_idx: indices exceed int32");
+  const long long n = (long long)B * S * (n_win + n_comp);
+  if (n == 0) return 0;
+  if (!out) return si::fail("hca_build_idx: null output");
+  si::hca_build_idx_kernel<<<si::elementwise_grid(n), 256, 0, stream>>>(B, S, n_win, n_comp, m_prime, out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : si::fail_cuda("hca_build_idx: launch", e);
+}
+
+}  // extern "C"

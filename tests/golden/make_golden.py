@@ -121,7 +121,20 @@ def main():
     built = plain(C.build_csa_topk_idxs(sc, 8, 16, seq_len=40, n_compressed=10, m=4, device="cpu"))
     out["csa_idx"] = dict(scores=sc, n_win=8, top_k=16, m=4, idx=built)
 
+    # 4. HCA forward (flash_sparse/reference.py:411-452): window + all legal compressed blocks
+    g2 = torch.Generator("cpu").manual_seed(13)
+    Bh, Sh, Hh, Dh, mp, nw = 1, 40, 8, 64, 8, 6
+    qh = (torch.randn((Bh, Sh, Hh, Dh), generator=g2) * Dh ** -0.5).bfloat16()
+    kvh = torch.randn((Bh, Sh, Dh), generator=g2).bfloat16()
+    kvc = torch.randn((Bh, Sh // mp, Dh), generator=g2).bfloat16()
+    sinkh = torch.randn(Hh, generator=g2)
+    oh = plain(R.reference_hca_forward(fx(qh.float()), fx(kvh.float()), fx(kvc.float()), fx(sinkh), nw, m_prime=mp))
+    out["hca"] = dict(q=qh, kv=kvh, kv_c=kvc, sink=sinkh, n_win=nw, m_prime=mp, o=oh.float())
+
+    only = os.environ.get("GOLDEN_ONLY")
     for name, d in out.items():
+        if only and name not in only.split(","):
+            continue
         torch.save(d, os.path.join(HERE, f"{name}.pt"))
         print("wrote", name)
 

@@ -69,3 +69,34 @@ def test_flash_csa_forward_small(d_v):
     ro, _, _ = oracle.csa_forward(q, x_kv, kvc.cpu(), q_idx, kc.cpu(), w, sink, nwin, k, m, d_v=d_v)
     assert o.shape == ro.shape
     assert (o.float().cpu() - ro).abs().max().item() <= 2e-2
+
+
+def test_hca_golden_and_oracle(golden):
+    from streamindex_b200.hca import build_hca_topk_idxs, flash_hca_forward
+
+    d = golden("hca")
+    B, S = d["q"].shape[:2]
+    nc = d["kv_c"].shape[1]
+    idx = build_hca_topk_idxs(B=B, seq_len=S, n_win=d["n_win"], n_compressed=nc, m_prime=d["m_prime"],
+                              device="cuda").cpu()
+    assert torch.equal(idx, oracle.build_hca_topk_idxs(B, S, d["n_win"], nc, d["m_prime"]))
+    o = flash_hca_forward(d["q"].cuda(), d["kv"].cuda(), d["kv_c"].cuda(), d["sink"].cuda(), n_win=d["n_win"],
+                          m_prime=d["m_prime"])
+    torch.cuda.synchronize()
+    assert (o.float().cpu() - d["o"]).abs().max().item() <= 2e-2
+
+
+def test_hca_v4_dims():
+    """HCA at V4 dims (D=576/512, m'=128, n_win=128) against the oracle."""
+    from streamindex_b200.hca import flash_hca_forward
+
+    B, S, H, D, mp, nw = 1, 1024, 64, 576, 128, 128
+    g = torch.Generator().manual_seed(17)
+    q = (torch.randn((B, S, H, D), generator=g) * D ** -0.5).bfloat16()
+    kv = (torch.randn((B, S, D), generator=g) * D ** -0.5).bfloat16()
+    kvc = (torch.randn((B, S // mp, D), generator=g) * D ** -0.5).bfloat16()
+    sink = torch.zeros(H)
+    o = flash_hca_forward(q.cuda(), kv.cuda(), kvc.cuda(), sink.cuda(), n_win=nw, m_prime=mp, d_v=512)
+    torch.cuda.synchronize()
+    ro, _, _ = oracle.hca_forward(q, kv, kvc, sink, nw, mp, d_v=512)
+    assert (o.float().cpu() - ro).abs().max().item() <= 2e-2

@@ -62,3 +62,11 @@ def test_compressor_window_and_csa_index(golden):
     nw = d["n_win"]
     assert torch.equal(got[..., :nw], ref[..., :nw])
     assert float(oracle.set_recall(ref[..., nw:], got[..., nw:]).min()) == 1.0
+
+
+def test_hca_forward_matches_reference(golden):
+    d = golden("hca")
+    o, _, idx = oracle.hca_forward(d["q"].float(), d["kv"].float(), d["kv_c"].float(), d["sink"], d["n_win"],
+                                   d["m_prime"])
+    torch.testing.assert_close(o, d["o"], rtol=1e-5, atol=1e-5)
+    assert idx.dtype == torch.int32
