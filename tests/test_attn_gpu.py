@@ -61,3 +61,35 @@ def test_large_score_range_rescales():
     idx = torch.arange(256, dtype=torch.int32).view(1, 1, -1).expand(1, 8, 256).contiguous() * 2
     # outputs reach ~18 here, where one bf16 ulp is 0.125: allow 1% relative on top of atol
     _check(q * 8, kv, sink, idx, rtol=1e-2)
+
+
+def test_config4_full_size_sampled_queries():
+    """BASELINE configs[3] at full size (S=65536, H=64, D=576/512, N_kv=16384,
+    K=512 causal random indices): outputs finite, all-masked rows zero, and
+    sampled queries spread over S match the oracle (atol 2e-2)."""
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    S, H, D, N, K = 65536, 64, 576, 16384, 512
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q = torch.randn((1, S, H, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    kv = torch.randn((1, N, D), generator=g, device=dev, dtype=torch.bfloat16)
+    sink = torch.zeros(H, device=dev)
+    # per query s: min(K, (s+1)//4) distinct indices from [0, (s+1)//4), -1 padded
+    idx = torch.full((1, S, K), -1, dtype=torch.int32, device=dev)
+    t = torch.arange(N, device=dev)
+    for s0 in range(0, S, 4096):
+        lim = torch.clamp((torch.arange(s0, s0 + 4096, device=dev) + 1) // 4, max=N)
+        rnd = torch.rand((4096, N), generator=g, device=dev).masked_fill(t.unsqueeze(0) >= lim.unsqueeze(1), -1.0)
+        v, i = rnd.topk(K, dim=-1)
+        idx[0, s0:s0 + 4096] = torch.where(v >= 0, i, torch.full_like(i, -1)).int()
+    o, lse = sparse_attn_fwd(q, kv, sink, idx, d_v=512)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(o.float()).all()) and bool(torch.isfinite(lse).all())
+    assert o[0, 0:3].abs().max().item() == 0.0  # queries 0..2 have no legal key
+    rows = [3, 1000, 4095, 20000, 40000, 65535]
+    for s_ in rows:
+        ro, _ = oracle.sparse_attn(q[:, s_:s_ + 1].cpu(), kv.cpu(), sink.cpu(), idx[:, s_:s_ + 1].cpu(), D ** -0.5,
+                                   d_v=512)
+        assert (o[:, s_:s_ + 1].float().cpu() - ro).abs().max().item() <= 2e-2

@@ -98,3 +98,47 @@ def test_run_host_pipelined_matches_device_path():
     for chunks in (1, 5):
         plan.run_host(hq, hk, hw, hi, hs, chunks=chunks)
         assert torch.equal(hi, di) and torch.equal(hs, dv)
+
+
+def test_full_size_config2_properties_and_sampled_rows():
+    """BASELINE configs[1] at its largest size, S=1,048,576 (T=262,144, k=512):
+    size-independent properties on every row (sorted descending, indices legal
+    under t < (s+1)//4 and distinct, exact valid counts min(k, (s+1)//4), pads
+    -1/-inf) plus exact oracle parity on sampled rows spread over S."""
+    from streamindex_b200.indexer import IndexerTopk
+
+    S, H, D, k, r = 1 << 20, 64, 128, 512, 4
+    T = S // r
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q = torch.randn((1, S, H, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    kk = torch.randn((1, T, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    w = torch.randn((1, S, H), generator=g, device=dev)
+    plan = IndexerTopk(1, S, T, H, D, k, causal_ratio=r, device=dev)
+    idx, sc = plan.run(q, kk, w)
+    torch.cuda.synchronize()
+    assert plan.status() == 0
+    s = torch.arange(S, device=dev).view(1, S, 1)
+    lim = torch.clamp((s + 1) // r, max=T)
+    valid = idx >= 0
+    assert torch.equal(valid.sum(-1, keepdim=True), torch.clamp(lim, max=k))
+    assert bool(((idx < lim) | ~valid).all())
+    assert torch.equal(valid, torch.isfinite(sc))
+    assert bool((sc[..., :-1] >= sc[..., 1:]).all())
+    srt, _ = torch.where(valid, idx, torch.full_like(idx, -1)).sort(dim=-1)
+    dup = (srt[..., 1:] == srt[..., :-1]) & (srt[..., 1:] >= 0)
+    assert not bool(dup.any())
+    # oracle on sampled rows (full key range of each)
+    rows = torch.tensor([5, 2047, 2048, 100003, 524287, 777777, S - 1])
+    kc = kk.cpu()
+    for s_ in rows.tolist():
+        qs = q[:, s_:s_ + 1].cpu()
+        ws = w[:, s_:s_ + 1].cpu()
+        n = min(T, (s_ + 1) // r)
+        sc_ref = oracle.lightning_indexer(qs, kc[:, :n], ws)
+        oi, ov = oracle.topk_desc_stable(sc_ref, min(k, n))
+        gi = idx[0, s_, : min(k, n)].cpu()
+        gv = sc[0, s_, : min(k, n)].cpu()
+        assert float(oracle.set_recall(oi.view(1, 1, -1), gi.view(1, 1, -1))) >= 0.995
+        assert oracle.score_close(gv, ov.view(-1), 1e-2)
