@@ -501,7 +501,8 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
 
         // ---- streaming top-k.  Every kSyncTiles tiles the half's four warps
         // meet: a query whose buffer could not absorb kSyncTiles more tiles of
-        // inserts is flushed by its owner warp, and thresholds are re-read.
+        // inserts is flushed by the slice (cooperative register select), and
+        // thresholds are re-read.
         // In between, inserts only need the cached threshold and an atomic.
         if (t % kSyncTiles == 0) {
           named_bar(1 + hf, 128);

@@ -18,23 +18,29 @@
 // inside the thread with no cross-thread reduction.  The two groups form a
 // double buffer: the epilogue of group 0 overlaps the MMAs of group 1.
 //
-// Warp roles (320 threads):
+// Warp roles (576 threads for H_I <= 64, 320 for H_I = 128):
 //   warp 0      TMA producer (Q block, K tiles)
 //   warp 1      TMEM allocator + single-thread UMMA issuer
-//   warps 2..9  epilogue: scores + streaming top-k.  Warp w reads TMEM lanes
-//               32*(w%4)..+32; warps 2-5 take columns [0,128) of each group,
-//               warps 6-9 columns [128,256).
+//   warps 2..   epilogue: scores + streaming top-k.  Warp w reads TMEM lanes
+//               32*(w%4)..+32 (its "quadrant"); the epilogue warps are cut into
+//               slices of four (one per quadrant) that own the same queries:
+//               64-column slices for H_I <= 64 (16 warps), 128-column slices
+//               for H_I = 128 (8 warps) — see EpiCfg.
 //
-// Streaming top-k.  Each query keeps, in a global workspace slab, a candidate
-// buffer of CAP 64-bit keys  key = ord(score) << 32 | (2^32-1 - t)  (larger
-// key = better under the reference's order).  A key enters the buffer iff it
-// beats the query's threshold key (the smallest key kept at the last flush,
-// 0 before).  When a buffer could overflow on the next tile, one warp runs an
-// exact radix select on it (8-bit digits over the 64-bit key), compacts it to
-// the top K and raises the threshold.  Selection is exact, so the result is
-// the exact top-K under the total order.  At the end of a query block the
-// kept keys are written unsorted into the idx output; a row-sort kernel turns
-// them into (idx int64, score fp32) sorted descending, padded with -1 / -inf.
+// Streaming top-k.  Each query keeps, in a global workspace slab (L2
+// resident), a candidate buffer of CAP 64-bit keys
+//   key = ord(score) << 32 | (2^32-1 - t)
+// (larger key = better under the reference's order).  A key enters the buffer
+// iff it beats the query's threshold key (the smallest key kept at the last
+// flush, 0 before; cached in registers).  Every kSyncTiles key tiles the
+// slice's four warps meet; a buffer that could not absorb kSyncTiles more
+// tiles of inserts is flushed: the four warps load it into registers, run an
+// exact radix select (8-bit digits over the 64-bit key, below the keys' common
+// prefix), compact it to the top K and raise the threshold.  Selection is
+// exact, so the result is the exact top-K under the total order whatever the
+// tiling.  At the end of a query block the kept keys are written unsorted into
+// the idx output; a row-sort kernel turns them into (idx int64, score fp32)
+// sorted descending, padded with -1 / -inf.
 #pragma once
 #include "ptx.cuh"
 

@@ -9,9 +9,8 @@
 //
 // Mapping.  One persistent CTA per SM walks work items (b, s, 64-head group).
 // Q [64 heads x D] stays in shared memory for the item; the item's selected
-// KV rows are gathered NK at a time with TMA row gathers (tile::gather4, one
-// 1152-byte row per index at D=576) into 128-byte-swizzled tiles that serve
-// both GEMMs:
+// KV rows (1152 bytes per index at D=576) are gathered NK at a time into
+// 128-byte-swizzled tiles that serve both GEMMs:
 //   MMA1  S[64 x NK]  = Q . KV^T           (M=64, K=D, A and B K-major)
 //   MMA2  O[64 x Dv] += P . V              (M=64, K=NK, P K-major, V MN-major)
 // With M=64 an accumulator occupies TMEM lanes 0-15 of each 32-lane quarter;
@@ -26,8 +25,11 @@
 // shift) <= 256 stays exact in bf16 range.  P goes to shared memory (bf16) as
 // the A operand of MMA2.
 //
-// Warp roles (192 threads): warp 0 TMA (Q + gathers), warp 1 TMEM alloc +
-// UMMA issue, warps 2-5 softmax / correction / output.
+// Warp roles (480 threads): warp 0 TMA for the Q tile, warp 1 TMEM alloc +
+// UMMA issue, warps 2-5 softmax / O correction / output, warps 6-13 kv row
+// gathers with 16-byte cp.async (completion signalled on the stage barrier with
+// cp.async.mbarrier.arrive.noinc), warp 14 TMA gather4 for the first atoms of
+// each row (single kv tensor only).
 #include <cuda_bf16.h>
 
 #include "capi_common.h"
