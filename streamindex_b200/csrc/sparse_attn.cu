@@ -22,7 +22,7 @@
 // the same head's O row.  The running shift is only raised when the tile max
 // exceeds it by more than 8 (log2 units), so O is rescaled (ld/scale/st with
 // the 16x32bx2 TMEM shape, which touches lanes 0-15 only) rarely; P = exp2(s -
-// shift) <= 256 stays exact in bf16 range.  P goes to shared memory (bf16) as
+// shift) <= 256 stays well inside the bf16 range.  P goes to shared memory (bf16) as
 // the A operand of MMA2.
 //
 // Warp roles (480 threads): warp 0 TMA for the Q tile, warp 1 TMEM alloc +
