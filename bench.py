@@ -551,13 +551,14 @@ def main():
             a.S = 65536
         run_attn(a)
         return
-    world, rank, local = init_dist()
     if a.impl == "reference":
+        # CPU-only arm: rank 0 alone measures on the host cores; other ranks exit
+        # at once (no process group, so nothing spins beside the measurement)
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
         run_reference(a, world, rank)
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
         return
+    world, rank, local = init_dist()
     line, (q, k, w, s_lo, device) = run_ours(a, world, rank, local)
     e2e = None if a.no_e2e else run_e2e(a, world, rank, q, k, w, s_lo, device)
     if rank == 0:
