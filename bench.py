@@ -492,51 +492,76 @@ def run_attn(a):
     print(json.dumps(line), flush=True)
 
 
-def run_csa(a):
+def run_csa(a, world=1, rank=0, local=0):
     """CSA layer forward, B=2, S=131072, H=64, D=576/512, H_I=64, D_I=128, m=4, k=512, n_win=128.
 
     One step = mean-pool compressor (kv and indexer keys) -> fused indexer + top-k
-    -> index build -> sparse attention, through flash_csa_forward."""
-    from streamindex_b200.csa import flash_csa_forward, mean_pool_compress
+    -> index build -> sparse attention.  With N GPUs the query range is
+    S-sharded (work-balanced slices): rank 0 compresses and broadcasts the
+    compressed kv / keys, every rank runs its slice (``csa_forward_slice``) and
+    the outputs are gathered to rank 0."""
+    from streamindex_b200.csa import csa_forward_slice, flash_csa_forward, mean_pool_compress
+    from streamindex_b200.dist import balanced_bounds, broadcast_keys, gather_to_rank0
 
     B, S, H, D, DV, HI, DI, m, k, nwin = 2, a.S, 64, 576, 512, 64, 128, 4, 512, 128
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", local)
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     x_kv = torch.randn((B, S, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
     x_k = torch.randn((B, S, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
-    q = torch.randn((B, S, H, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
-    q_idx = torch.randn((B, S, HI, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
-    w = torch.randn((B, S, HI), generator=g, device=dev, dtype=torch.float32)
+    # attention work per query relative to one indexer key: (n_win + k) * H * (D + DV) vs H_I * D_I flops
+    extra = (nwin + k) * H * (D + DV) / (HI * DI)
+    bounds = balanced_bounds(S, world, S // m, m, align=128, extra_per_query=extra)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(100 + rank)
+    q = torch.randn((B, hi - lo, H, D), generator=gq, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    q_idx = torch.randn((B, hi - lo, HI, DI), generator=gq, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
+    w = torch.randn((B, hi - lo, HI), generator=gq, device=dev, dtype=torch.float32)
     sink = torch.zeros(H, dtype=torch.float32, device=dev)
+    kvc = torch.empty((B, S // m, D), dtype=torch.bfloat16, device=dev)
+    kc = torch.empty((B, S // m, DI), dtype=torch.bfloat16, device=dev)
+    full = torch.empty((B, S, H, DV), dtype=torch.bfloat16, device=dev) if (world > 1 and rank == 0) else None
 
     def step():
-        kvc = mean_pool_compress(x_kv, m)
-        kc = mean_pool_compress(x_k, m)
-        return flash_csa_forward(q, x_kv, kvc, q_idx, kc, w, sink, n_win=nwin, top_k=k, m=m, d_v=DV)
+        if world == 1:
+            kvc.copy_(mean_pool_compress(x_kv, m))
+            kc.copy_(mean_pool_compress(x_k, m))
+            return flash_csa_forward(q, x_kv, kvc, q_idx, kc, w, sink, n_win=nwin, top_k=k, m=m, d_v=DV)
+        if rank == 0:
+            kvc.copy_(mean_pool_compress(x_kv, m))
+            kc.copy_(mean_pool_compress(x_k, m))
+        broadcast_keys(kvc)
+        broadcast_keys(kc)
+        o = csa_forward_slice(q, x_kv, kvc, q_idx, kc, w, sink, s_offset=lo, n_win=nwin, top_k=k, m=m, d_v=DV)
+        gather_to_rank0(o, bounds, full, dim=1)
+        return o
 
     for _ in range(a.warmup):
         step()
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(local)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
+    _barrier_sync(world)
     clocks.start()
     t0.record()
     for _ in range(a.steps):
         step()
     t1.record()
-    torch.cuda.synchronize()
+    _barrier_sync(world)
     clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / a.steps
-    line = {
-        "metric": "CSA layer forward (BASELINE configs[4]) Mqueries/s", "value": B * S / (ms * 1e-3) / 1e6,
-        "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"flash_csa_forward B=2 S={S} H=64 D=576/512 H_I=64 D_I=128 m=4 top_k=512 n_win=128",
-                   "path": "mean-pool x2 -> fused indexer+top-k -> index build -> split-kv sparse attention"},
-        "clocks": clk,
-    }
-    print(json.dumps(line), flush=True)
+    ms = _max_over_ranks(t0.elapsed_time(t1) / a.steps, world, dev)
+    if rank == 0:
+        line = {
+            "metric": "CSA layer forward (BASELINE configs[4]) Mqueries/s", "value": B * S / (ms * 1e-3) / 1e6,
+            "unit": "Mqueries/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"flash_csa_forward B=2 S={S} H=64 D=576/512 H_I=64 D_I=128 m=4 top_k=512 n_win=128",
+                       "path": "mean-pool x2 -> fused indexer+top-k -> index build -> split-kv sparse attention",
+                       "parallelism": f"S-shard x{world} (compressed kv/keys broadcast, output gathered)"
+                       if world > 1 else "single GPU"},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
 
 
 def main():
@@ -544,7 +569,11 @@ def main():
     if a.workload == "csa":
         if a.S == 1 << 20:
             a.S = 131072
-        run_csa(a)
+        world, rank, local = init_dist()
+        run_csa(a, world, rank, local)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
         return
     if a.workload == "attn":
         if a.S == 1 << 20:

@@ -140,6 +140,13 @@ SI_API int si_scores_topk(const float* scores, int B, int S, int T, int top_k, i
 SI_API int si_csa_build_idx(const int64_t* comp_idx, int B, int S, int top_k, int n_win, int32_t* out,
                             cudaStream_t stream);
 
+/* si_csa_build_idx for a query slice: local rows [0,S) are global positions
+ * s_offset + s of a sequence of S_total tokens (window and causality use the
+ * global position; compressed picks are offset by S_total).  Used by the
+ * S-sharded CSA forward. */
+SI_API int si_csa_build_idx_ex(const int64_t* comp_idx, int B, int S, long long s_offset, int S_total, int top_k,
+                               int n_win, int32_t* out, cudaStream_t stream);
+
 /* HCA attention index list [B,S,n_win+n_comp] int32: sliding window, then all
  * compressed blocks legal for the query ((i+1)*m_prime - 1 <= s) offset by S,
  * else -1.  Replaces build_hca_topk_idxs (flash_sparse/hca.py:24-51). */

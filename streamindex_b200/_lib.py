@@ -41,6 +41,8 @@ SIGNATURES = {
     "si_scores_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
                                c_void_p]),
     "si_csa_build_idx": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "si_csa_build_idx_ex": (c_int, [c_void_p, c_int, c_int, ctypes.c_longlong, c_int, c_int, c_int, c_void_p,
+                                    c_void_p]),
     "si_hca_build_idx": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "si_mean_pool": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "si_indexer_score": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,

@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 from .attention import _attn_call
-from .indexer import chunked_indexer_topk
+from .indexer import chunked_indexer_topk, indexer_topk_slice
 
 
 def sliding_window_idxs(B: int, S: int, n_win: int, device) -> torch.Tensor:
@@ -127,6 +127,46 @@ def flash_csa_forward(
         softmax_scale = d ** -0.5
     comp, _ = chunked_indexer_topk(q_idx, k_idx_compressed, indexer_weights, top_k, causal_ratio=m)
     idx = csa_index_list(comp, n_win)
+    dv = d if d_v is None else int(d_v)
+    o, _ = _attn_call(q, kv, kv_compressed, attn_sink, idx, softmax_scale, dv)
+    return o
+
+
+def csa_forward_slice(
+    q: torch.Tensor,
+    kv: torch.Tensor,
+    kv_compressed: torch.Tensor,
+    q_idx: torch.Tensor,
+    k_idx_compressed: torch.Tensor,
+    indexer_weights: torch.Tensor,
+    attn_sink: torch.Tensor,
+    *,
+    s_offset: int,
+    n_win: int,
+    top_k: int,
+    m: int = 4,
+    softmax_scale: Optional[float] = None,
+    d_v: Optional[int] = None,
+) -> torch.Tensor:
+    """CSA forward for the query slice ``[s_offset, s_offset + q.shape[1])`` of a sequence.
+
+    ``q`` / ``q_idx`` / ``indexer_weights`` hold only the slice; ``kv`` (all
+    ``S_total`` tokens), ``kv_compressed`` and ``k_idx_compressed`` are full.
+    Causality, the window and the compressed offset use global positions, so
+    concatenating the slices' outputs equals :func:`flash_csa_forward` on the
+    whole sequence.  This is what each rank runs in the S-sharded CSA forward.
+    """
+    B, S_loc, n_h, d = q.shape
+    S_total = kv.shape[1]
+    if softmax_scale is None:
+        softmax_scale = d ** -0.5
+    comp, _ = indexer_topk_slice(q_idx, k_idx_compressed, indexer_weights, top_k, m, s_offset)
+    comp = comp.contiguous()
+    idx = torch.empty((B, S_loc, n_win + top_k), dtype=torch.int32, device=q.device)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(lib.si_csa_build_idx_ex(comp.data_ptr(), B, S_loc, int(s_offset), S_total, top_k, int(n_win),
+                                           idx.data_ptr(), _lib.stream_handle(q.device)))
     dv = d if d_v is None else int(d_v)
     o, _ = _attn_call(q, kv, kv_compressed, attn_sink, idx, softmax_scale, dv)
     return o

@@ -13,21 +13,21 @@ namespace si {
 // (flash_sparse/reference.py:470-475); compressed indices are offset by S
 // because the attention reads cat[kv; kv_compressed] (flash_sparse/csa.py:177-179).
 __global__ void csa_build_idx_kernel(const int64_t* __restrict__ comp, int B, int S, int top_k, int n_win,
-                                     int32_t* __restrict__ out) {
+                                     long long s_offset, int S_total, int32_t* __restrict__ out) {
   const int W = n_win + top_k;
   const long long total = (long long)B * S * W;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const int col = (int)(i % W);
     const long long bs = i / W;
-    const int s = (int)(bs % S);
+    const long long s = s_offset + bs % S;  // global query position
     int v;
     if (col < n_win) {
-      const int pos = s - n_win + 1 + col;
-      v = (pos >= 0 && pos <= s) ? pos : -1;
+      const long long pos = s - n_win + 1 + col;
+      v = (pos >= 0 && pos <= s) ? (int)pos : -1;
     } else {
       const long long c = comp[bs * top_k + (col - n_win)];
-      v = c >= 0 ? (int)(c + S) : -1;
+      v = c >= 0 ? (int)(c + S_total) : -1;
     }
     out[i] = v;
   }
@@ -69,15 +69,22 @@ static int elementwise_grid(long long n) {
 
 extern "C" {
 
-int si_csa_build_idx(const int64_t* comp_idx, int B, int S, int top_k, int n_win, int32_t* out, cudaStream_t stream) {
-  if (B < 1 || S < 0 || top_k < 0 || n_win < 0) return si::fail("csa_build_idx: bad sizes");
-  if ((long long)S + 1 >= (1ll << 31)) return si::fail("csa_build_idx: S too large for int32 indices");
+int si_csa_build_idx_ex(const int64_t* comp_idx, int B, int S, long long s_offset, int S_total, int top_k, int n_win,
+                        int32_t* out, cudaStream_t stream) {
+  if (B < 1 || S < 0 || top_k < 0 || n_win < 0 || s_offset < 0 || s_offset + S > S_total)
+    return si::fail("csa_build_idx: bad sizes (S=%d, s_offset=%lld, S_total=%d)", S, s_offset, S_total);
+  if ((long long)S_total * 2 + 1 >= (1ll << 31)) return si::fail("csa_build_idx: S too large for int32 indices");
   const long long n = (long long)B * S * (n_win + top_k);
   if (n == 0) return 0;
   if (!out || (top_k > 0 && !comp_idx)) return si::fail("csa_build_idx: null pointer");
-  si::csa_build_idx_kernel<<<si::elementwise_grid(n), 256, 0, stream>>>(comp_idx, B, S, top_k, n_win, out);
+  si::csa_build_idx_kernel<<<si::elementwise_grid(n), 256, 0, stream>>>(comp_idx, B, S, top_k, n_win, s_offset,
+                                                                          S_total, out);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : si::fail_cuda("csa_build_idx: launch", e);
+}
+
+int si_csa_build_idx(const int64_t* comp_idx, int B, int S, int top_k, int n_win, int32_t* out, cudaStream_t stream) {
+  return si_csa_build_idx_ex(comp_idx, B, S, 0, S, top_k, n_win, out, stream);
 }
 
 int si_mean_pool(const void* x, int B, int S, int C, int m, void* out, cudaStream_t stream) {

@@ -31,13 +31,18 @@ def legal_pairs(S: int, T: int, ratio: Optional[int], lo: int = 0, hi: Optional[
     return int(np.minimum(T, (s + 1) // int(ratio)).sum())
 
 
-def balanced_bounds(S: int, N: int, T: int, ratio: Optional[int], align: int = 128) -> List[int]:
-    """N+1 boundaries, multiples of ``align`` (except S), splitting the legal pairs evenly."""
+def balanced_bounds(S: int, N: int, T: int, ratio: Optional[int], align: int = 128,
+                    extra_per_query: float = 0.0) -> List[int]:
+    """N+1 boundaries, multiples of ``align`` (except S), splitting the work evenly.
+
+    Work of query s = its legal key count ``min(T, (s+1)//ratio)`` plus
+    ``extra_per_query`` (work that does not grow with s, e.g. the attention of a
+    CSA layer, in the same units)."""
     if N <= 1:
         return [0, S]
     s = np.arange(S, dtype=np.int64)
     w = np.minimum(T, (s + 1) // int(ratio)) if ratio else np.full(S, T, dtype=np.int64)
-    w = np.maximum(w, 1)  # every query costs at least its output write
+    w = np.maximum(w.astype(np.float64) + float(extra_per_query), 1.0)  # every query costs at least its output
     cum = np.cumsum(w)
     total = int(cum[-1])
     bounds = [0]
@@ -66,14 +71,22 @@ def gather_to_rank0(local: torch.Tensor, bounds: List[int], full: Optional[torch
     if rank == 0:
         assert full is not None
         full.narrow(dim, bounds[0], bounds[1] - bounds[0]).copy_(local)
+        staged = []
         for r in range(1, world):
             n = bounds[r + 1] - bounds[r]
             if n > 0:
-                ops.append(dist.P2POp(dist.irecv, full.narrow(dim, bounds[r], n), r))
+                view = full.narrow(dim, bounds[r], n)
+                buf = view if view.is_contiguous() else torch.empty(view.shape, dtype=view.dtype, device=view.device)
+                if buf is not view:
+                    staged.append((view, buf))
+                ops.append(dist.P2POp(dist.irecv, buf, r))
     else:
         if local.numel() > 0:
             ops.append(dist.P2POp(dist.isend, local.contiguous(), 0))
     if ops:
         for req in dist.batch_isend_irecv(ops):
             req.wait()
+    if rank == 0:
+        for view, buf in staged:
+            view.copy_(buf)
     return full

@@ -70,6 +70,25 @@ def _topk(q, k_idx, weights, top_k: int, width: int, ratio: Optional[int], mask:
     return out_idx, out_scores
 
 
+def indexer_topk_slice(q, k_idx, weights, top_k: int, causal_ratio: int, s_offset: int):
+    """Indexer + top-k for the query slice starting at global position ``s_offset``
+    (causal limit ``t < (s_offset + s + 1)//causal_ratio``).  Returns ``(idx, scores)``."""
+    q, k_idx, weights, (B, S, H, D, T) = _prep(q, k_idx, weights)
+    dev = q.device
+    out_idx = torch.empty((B, S, top_k), dtype=torch.int64, device=dev)
+    out_scores = torch.empty((B, S, top_k), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws_bytes = lib.si_indexer_topk_ws_bytes(B, S, T, H, D, top_k)
+    with torch.cuda.device(dev):
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        _lib.check(lib.si_indexer_topk_ex(
+            q.data_ptr(), k_idx.data_ptr(), weights.data_ptr(), int(weights.dtype == torch.bfloat16),
+            int(q.dtype == torch.float16), B, S, T, H, D, int(top_k), int(causal_ratio), None, int(s_offset), 0,
+            out_idx.data_ptr(), out_scores.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_handle(dev)))
+        _lib.maybe_check_status(ws, dev, "indexer_topk")
+    return out_idx, out_scores
+
+
 def chunked_indexer_topk(
     q: torch.Tensor,
     k_idx: torch.Tensor,

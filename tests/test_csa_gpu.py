@@ -100,3 +100,26 @@ def test_hca_v4_dims():
     torch.cuda.synchronize()
     ro, _, _ = oracle.hca_forward(q, kv, kvc, sink, nw, mp, d_v=512)
     assert (o.float().cpu() - ro).abs().max().item() <= 2e-2
+
+
+def test_csa_forward_slices_equal_whole_sequence():
+    """S-sharding: per-slice CSA forwards (global offsets) concatenate to the
+    whole-sequence forward exactly (same kernels, same inputs per query)."""
+    from streamindex_b200.csa import csa_forward_slice, flash_csa_forward, mean_pool_compress
+    from streamindex_b200.dist import balanced_bounds
+
+    B, S, H, D, HI, DI, m, nwin, k = 2, 512, 64, 576, 64, 128, 4, 16, 32
+    g = torch.Generator().manual_seed(5)
+    q = (torch.randn((B, S, H, D), generator=g) * D ** -0.5).bfloat16().cuda()
+    x_kv = (torch.randn((B, S, D), generator=g) * D ** -0.5).bfloat16().cuda()
+    q_idx = (torch.randn((B, S, HI, DI), generator=g) * DI ** -0.5).bfloat16().cuda()
+    x_k = (torch.randn((B, S, DI), generator=g) * DI ** -0.5).bfloat16().cuda()
+    w = torch.randn((B, S, HI), generator=g).cuda()
+    sink = torch.randn(H, generator=g).cuda()
+    kvc, kc = mean_pool_compress(x_kv, m), mean_pool_compress(x_k, m)
+    full = flash_csa_forward(q, x_kv, kvc, q_idx, kc, w, sink, n_win=nwin, top_k=k, m=m, d_v=512)
+    bounds = balanced_bounds(S, 3, S // m, m, align=64, extra_per_query=nwin + k)
+    parts = [csa_forward_slice(q[:, a:b], x_kv, kvc, q_idx[:, a:b], kc, w[:, a:b], sink, s_offset=a, n_win=nwin,
+                               top_k=k, m=m, d_v=512) for a, b in zip(bounds, bounds[1:])]
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(parts, dim=1), full)
