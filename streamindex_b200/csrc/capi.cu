@@ -62,6 +62,19 @@ int make_tmap_2d_16b(CUtensorMap* map, const void* base, int cols, uint64_t rows
   return 0;
 }
 
+cudaError_t set_smem_attr_once(const void* func, int bytes, unsigned long long* seen) {
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  std::lock_guard<std::mutex> lock(mu);
+  if (*seen & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) *seen |= bit;
+  return e;
+}
+
 __global__ void fill_pad_kernel(int64_t* idx, float* scores, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     idx[i] = -1;

@@ -17,6 +17,9 @@ int device_sm_count();
 // [box_rows, box_cols] with the 128-byte swizzle.  dtype: 0 bf16, 1 fp16.
 int make_tmap_2d_16b(CUtensorMap* map, const void* base, int cols, uint64_t rows, int box_cols, int box_rows,
                      int dtype);
+// Sets a kernel's max dynamic shared memory once per (kernel, device); thread safe.
+// `seen` is a per-kernel bitmask of devices already configured.
+cudaError_t set_smem_attr_once(const void* func, int bytes, unsigned long long* seen);
 cudaError_t launch_fill_pad(int64_t* idx, float* scores, long long n, cudaStream_t stream);
 
 }  // namespace si

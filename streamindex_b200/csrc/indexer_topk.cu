@@ -828,13 +828,10 @@ template <int H, int MODE>
 static cudaError_t launch_indexer_t(const CUtensorMap& mq, const CUtensorMap& mk, const IndexerParams& p, int grid,
                                     uint32_t idesc, cudaStream_t stream) {
   const size_t smem = indexer_smem_bytes(p.D);
-  static bool configured = false;  // one-time attribute set, idempotent
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(indexer_topk_kernel<H, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)indexer_smem_bytes(128));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static unsigned long long configured = 0;  // devices on which the attribute is set
+  cudaError_t e = set_smem_attr_once(reinterpret_cast<const void*>(indexer_topk_kernel<H, MODE>),
+                                     (int)indexer_smem_bytes(128), &configured);
+  if (e != cudaSuccess) return e;
   indexer_topk_kernel<H, MODE><<<grid, EpiCfg<H>::THREADS, smem, stream>>>(mq, mk, p, idesc);
   return cudaGetLastError();
 }

@@ -553,13 +553,10 @@ template <int DVH>
 static cudaError_t launch_t(const CUtensorMap& mq, const CUtensorMap& mkv, const Params& p, int grid,
                             cudaStream_t stream) {
   constexpr int NK = 32;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(sparse_attn_fwd_kernel<NK, DVH>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static unsigned long long configured = 0;  // devices on which the attribute is set
+  cudaError_t e = set_smem_attr_once(reinterpret_cast<const void*>(sparse_attn_fwd_kernel<NK, DVH>), kSmemMax,
+                                     &configured);
+  if (e != cudaSuccess) return e;
   sparse_attn_fwd_kernel<NK, DVH><<<grid, kThreads, smem_bytes<NK>(p.NA), stream>>>(mq, mkv, p);
   return cudaGetLastError();
 }

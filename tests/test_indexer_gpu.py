@@ -142,3 +142,14 @@ def test_full_size_config2_properties_and_sampled_rows():
         gv = sc[0, s_, : min(k, n)].cpu()
         assert float(oracle.set_recall(oi.view(1, 1, -1), gi.view(1, 1, -1))) >= 0.995
         assert oracle.score_close(gv, ov.view(-1), 1e-2)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_devices_one_process():
+    """Kernel attributes are set per device: the same process can run on cuda:0 then cuda:1."""
+    import streamindex_b200 as si
+
+    q, kk, w = oracle.indexer_inputs(1, 256, 64, 128, 64, seed=8)
+    out = [si.chunked_indexer_topk(q.to(d), kk.to(d), w.to(d), 16, causal_ratio=4)[0].cpu()
+           for d in ("cuda:0", "cuda:1")]
+    assert torch.equal(out[0], out[1])
