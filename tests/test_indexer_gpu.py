@@ -153,3 +153,35 @@ def test_two_devices_one_process():
     out = [si.chunked_indexer_topk(q.to(d), kk.to(d), w.to(d), 16, causal_ratio=4)[0].cpu()
            for d in ("cuda:0", "cuda:1")]
     assert torch.equal(out[0], out[1])
+
+
+@pytest.mark.parametrize("H,D", [(16, 64), (128, 128)])
+def test_indexer_score_other_heads(H, D):
+    import streamindex_b200 as si
+
+    q, kk, w = oracle.indexer_inputs(2, 70, H, D, 150, seed=H)
+    got = si.indexer_score(q.cuda(), kk.cuda(), w.cuda()).cpu()
+    ref = oracle.lightning_indexer(q, kk, w)
+    assert oracle.score_close(got, ref, 1e-2)
+
+
+def test_indexer_score_topk_width_and_mask():
+    """indexer_score_topk returns width min(top_k, T); -1/-inf where no legal key."""
+    import streamindex_b200 as si
+
+    q, kk, w = oracle.indexer_inputs(1, 64, 64, 128, 40, seed=31)
+    cm = torch.rand((1, 64, 40), generator=torch.Generator().manual_seed(3)) < 0.5
+    gi, gv = si.indexer_score_topk(q.cuda(), kk.cuda(), w.cuda(), 100, causal_mask=cm.cuda())
+    assert gi.shape == (1, 64, 40)
+    oi, ov = oracle.materialize_topk(q, kk, w, 100, causal_mask=cm, pad=False)
+    _assert_parity(gi.cpu(), gv.cpu(), oi, ov)
+
+
+def test_indexer_fp16_operands():
+    import streamindex_b200 as si
+
+    q, kk, w = oracle.indexer_inputs(1, 256, 64, 128, 64, seed=41)
+    q16, k16 = q.float().half(), kk.float().half()
+    gi, gv = si.chunked_indexer_topk(q16.cuda(), k16.cuda(), w.cuda(), 24, causal_ratio=4)
+    oi, ov = oracle.materialize_topk(q16, k16, w, 24, ratio=4)
+    _assert_parity(gi.cpu(), gv.cpu(), oi, ov)
