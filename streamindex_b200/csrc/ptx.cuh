@@ -233,13 +233,11 @@ namespace si {
 // Two 32-column TMEM loads and the wait in one asm statement, so no use of the
 // destination registers can be scheduled before tcgen05.wait::ld.
 __device__ __forceinline__ void tmem_ld32x2_sync(uint32_t taddr0, uint32_t taddr1, float (&va)[32], float (&vb)[32]) {
-  uint32_t* a = reinterpret_cast<uint32_t*>(va);
-  uint32_t* b = reinterpret_cast<uint32_t*>(vb);
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(a[0]),"=r"(a[1]),"=r"(a[2]),"=r"(a[3]),"=r"(a[4]),"=r"(a[5]),"=r"(a[6]),"=r"(a[7]),"=r"(a[8]),"=r"(a[9]),"=r"(a[10]),"=r"(a[11]),"=r"(a[12]),"=r"(a[13]),"=r"(a[14]),"=r"(a[15]),"=r"(a[16]),"=r"(a[17]),"=r"(a[18]),"=r"(a[19]),"=r"(a[20]),"=r"(a[21]),"=r"(a[22]),"=r"(a[23]),"=r"(a[24]),"=r"(a[25]),"=r"(a[26]),"=r"(a[27]),"=r"(a[28]),"=r"(a[29]),"=r"(a[30]),"=r"(a[31]),"=r"(b[0]),"=r"(b[1]),"=r"(b[2]),"=r"(b[3]),"=r"(b[4]),"=r"(b[5]),"=r"(b[6]),"=r"(b[7]),"=r"(b[8]),"=r"(b[9]),"=r"(b[10]),"=r"(b[11]),"=r"(b[12]),"=r"(b[13]),"=r"(b[14]),"=r"(b[15]),"=r"(b[16]),"=r"(b[17]),"=r"(b[18]),"=r"(b[19]),"=r"(b[20]),"=r"(b[21]),"=r"(b[22]),"=r"(b[23]),"=r"(b[24]),"=r"(b[25]),"=r"(b[26]),"=r"(b[27]),"=r"(b[28]),"=r"(b[29]),"=r"(b[30]),"=r"(b[31])
+      : "=f"(va[0]),"=f"(va[1]),"=f"(va[2]),"=f"(va[3]),"=f"(va[4]),"=f"(va[5]),"=f"(va[6]),"=f"(va[7]),"=f"(va[8]),"=f"(va[9]),"=f"(va[10]),"=f"(va[11]),"=f"(va[12]),"=f"(va[13]),"=f"(va[14]),"=f"(va[15]),"=f"(va[16]),"=f"(va[17]),"=f"(va[18]),"=f"(va[19]),"=f"(va[20]),"=f"(va[21]),"=f"(va[22]),"=f"(va[23]),"=f"(va[24]),"=f"(va[25]),"=f"(va[26]),"=f"(va[27]),"=f"(va[28]),"=f"(va[29]),"=f"(va[30]),"=f"(va[31]),"=f"(vb[0]),"=f"(vb[1]),"=f"(vb[2]),"=f"(vb[3]),"=f"(vb[4]),"=f"(vb[5]),"=f"(vb[6]),"=f"(vb[7]),"=f"(vb[8]),"=f"(vb[9]),"=f"(vb[10]),"=f"(vb[11]),"=f"(vb[12]),"=f"(vb[13]),"=f"(vb[14]),"=f"(vb[15]),"=f"(vb[16]),"=f"(vb[17]),"=f"(vb[18]),"=f"(vb[19]),"=f"(vb[20]),"=f"(vb[21]),"=f"(vb[22]),"=f"(vb[23]),"=f"(vb[24]),"=f"(vb[25]),"=f"(vb[26]),"=f"(vb[27]),"=f"(vb[28]),"=f"(vb[29]),"=f"(vb[30]),"=f"(vb[31])
       : "r"(taddr0), "r"(taddr1)
       : "memory");
 }
