@@ -36,6 +36,12 @@ SI_API const char* si_last_error(void);
 /* Synchronises `stream` and copies the workspace's status word to *status_out. */
 SI_API int si_read_status(const void* ws, int* status_out, cudaStream_t stream);
 
+/* Self-test of the kernels' bounded waits: launches one CTA that waits on a
+ * barrier nothing arrives on; after limit_ns (<= 2 s) the wait gives up,
+ * writes status 1 (the "data never arrived" code) to the workspace status
+ * word and the kernel returns normally.  No counterpart in the reference. */
+SI_API int si_selftest_wait_timeout(void* ws, unsigned long long limit_ns, cudaStream_t stream);
+
 /* Workspace bytes for si_indexer_topk on the current device. */
 SI_API size_t si_indexer_topk_ws_bytes(int B, int S, int T, int H, int D, int top_k);
 

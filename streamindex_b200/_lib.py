@@ -22,6 +22,7 @@ SIGNATURES = {
     "si_abi_version": (c_int, []),
     "si_last_error": (c_char_p, []),
     "si_read_status": (c_int, [c_void_p, ctypes.POINTER(c_int), c_void_p]),
+    "si_selftest_wait_timeout": (c_int, [c_void_p, ctypes.c_ulonglong, c_void_p]),
     "si_indexer_topk_ws_bytes": (c_size_t, [c_int] * 6),
     "si_indexer_topk": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                 c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -5,6 +5,7 @@
 #include <mutex>
 
 #include "capi_common.h"
+#include "ptx.cuh"
 #include "../../include/streamindex_b200.h"
 
 namespace si {
@@ -90,9 +91,37 @@ cudaError_t launch_fill_pad(int64_t* idx, float* scores, long long n, cudaStream
   return cudaGetLastError();
 }
 
+// Self-test of the bounded-wait machinery: one CTA waits on an mbarrier that
+// nothing ever arrives on.  The wait must give up after `limit_ns`, record
+// kErrWaitTmaFull in the status word and let the kernel return normally.
+__global__ void wait_timeout_selftest_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  mbar_wait_ns(&bar, 0, &abort_flag, status, kErrWaitTmaFull, limit_ns);
+  __syncthreads();
+}
+
 }  // namespace si
 
 extern "C" {
+
+int si_selftest_wait_timeout(void* ws, unsigned long long limit_ns, cudaStream_t stream) {
+  if (!ws) return si::fail("selftest_wait_timeout: null workspace");
+  if (limit_ns > 2000000000ull) return si::fail("selftest_wait_timeout: limit above 2 s");
+  int* status = reinterpret_cast<int*>(ws);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return si::fail_cuda("selftest_wait_timeout: status reset", e);
+  si::wait_timeout_selftest_kernel<<<1, 64, 0, stream>>>(status, limit_ns);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : si::fail_cuda("selftest_wait_timeout: launch", e);
+}
+
 
 const char* si_last_error(void) { return si::g_err; }
 

@@ -108,20 +108,24 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Bounded wait.  Returns false (after recording `code`) on timeout or when
 // another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                             int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
     __nanosleep(SI_WAIT_BACKOFF_NS);  // poll sparsely: waiting warps yield their issue slots
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > SI_WAIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicCAS(status, 0, code);
       *abort_flag = 1;
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int code) {
+  return mbar_wait_ns(bar, parity, abort_flag, status, code, SI_WAIT_NS);
 }
 
 // ---------------------------------------------------------------- TMA
