@@ -139,6 +139,14 @@ SI_API size_t si_scores_topk_ws_bytes(int B, int S, int top_k);
 SI_API int si_scores_topk(const float* scores, int B, int S, int T, int top_k, int causal_ratio, int64_t* out_idx,
                           float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+/* si_scores_topk with an optional explicit [B,S,T] byte mask (nonzero = legal),
+ * applied together with the causal ratio (<= 0: none).  Replaces the
+ * masked_fill + topk of reference_csa_forward's causal_mask_for_compressed
+ * (flash_sparse/reference.py:389-397). */
+SI_API int si_scores_topk_mask(const float* scores, int B, int S, int T, int top_k, int causal_ratio,
+                               const uint8_t* causal_mask, int64_t* out_idx, float* out_scores, void* ws,
+                               size_t ws_bytes, cudaStream_t stream);
+
 /* CSA attention index list [B,S,n_win+top_k] int32: sliding window then
  * compressed picks offset by S (-1 kept).  Replaces _build_sliding_window_idxs
  * (flash_sparse/reference.py:460-475) + the concatenation of
@@ -157,6 +165,15 @@ SI_API int si_csa_build_idx_ex(const int64_t* comp_idx, int B, int S, long long 
  * compressed blocks legal for the query ((i+1)*m_prime - 1 <= s) offset by S,
  * else -1.  Replaces build_hca_topk_idxs (flash_sparse/hca.py:24-51). */
 SI_API int si_hca_build_idx(int B, int S, int n_win, int n_comp, int m_prime, int32_t* out, cudaStream_t stream);
+
+/* Softmax-gated token compressor [B,S,C] -> [B,S/m,C] (fp32 math; bf16 or fp32
+ * tensors).  Replaces reference_token_compressor (flash_sparse/reference.py:176-272):
+ * overlap = 0: weights softmax_m(z_a + b_a), b_a [m,C];
+ * overlap = 1: joint 2m-way softmax over the block's a-stream and the previous
+ *              block's b-stream (c_b, z_b, b_b [m,C]); block 0 has no b-stream. */
+SI_API int si_token_compressor(const void* c_a, const void* z_a, const void* b_a, const void* c_b, const void* z_b,
+                               const void* b_b, int B, int S, int C, int m, int overlap, int is_bf16, void* out,
+                               cudaStream_t stream);
 
 /* Mean-pool compressor [B,S,C] bf16 -> [B,S/m,C] bf16 (trailing S % m tokens
  * dropped).  Equals reference_token_compressor(overlap=False) with zero scores

@@ -30,6 +30,7 @@ from .csa import (  # noqa: F401
     csa_forward,
     build_hca_topk_idxs,
     hca_forward,
+    token_compressor,
 )
 from .metrics import set_recall, norm_corr, score_close  # noqa: F401
 from .inputs import indexer_inputs, attn_inputs  # noqa: F401

@@ -106,3 +106,33 @@ def hca_forward(q, kv, kv_compressed, attn_sink, n_win: int, m_prime: int, softm
     kv_full = torch.cat([kv, kv_compressed], dim=1)
     o, lse = sparse_attn(q, kv_full, attn_sink, idx, softmax_scale, d_v=d_v)
     return o, lse, idx
+
+
+def token_compressor(c_a, z_a, b_a, m, c_b=None, z_b=None, b_b=None, overlap=False):
+    """Softmax-gated pooling of m tokens per block (``flash_sparse/reference.py:176-272``).
+
+    overlap=False: ``softmax_m(z_a + b_a)`` weights over each block of m tokens.
+    overlap=True: a joint 2m-way softmax over the block's a-stream (``z_a + b_a``)
+    and the previous block's b-stream (``z_b + b_b``, -inf / zero value for block
+    0).  The shipped reference nests the overlap body under its shape check
+    (dead code); this restates the code as written there, un-nested.
+    Returns ``[B, S//m, c]`` in c_a's dtype (fp32 math).
+    """
+    B, S, c = c_a.shape
+    nb = S // m
+    if nb == 0:
+        return c_a.new_zeros(B, 0, c)
+    cut = nb * m
+    ca = c_a[:, :cut].float().reshape(B, nb, m, c)
+    za = z_a[:, :cut].float().reshape(B, nb, m, c) + b_a.float()
+    if not overlap:
+        return (ca * za.softmax(dim=2)).sum(dim=2).to(c_a.dtype)
+    cb = c_b[:, :cut].float().reshape(B, nb, m, c)
+    zb = z_b[:, :cut].float().reshape(B, nb, m, c) + b_b.float()
+    cbs = torch.zeros_like(cb)
+    cbs[:, 1:] = cb[:, :-1]
+    zbs = torch.full_like(zb, float("-inf"))
+    zbs[:, 1:] = zb[:, :-1]
+    cj = torch.cat([ca, cbs], dim=2)
+    zj = torch.cat([za, zbs], dim=2)
+    return (cj * zj.softmax(dim=2)).sum(dim=2).to(c_a.dtype)

@@ -41,10 +41,13 @@ SIGNATURES = {
     "si_scores_topk_ws_bytes": (c_size_t, [c_int, c_int, c_int]),
     "si_scores_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
                                c_void_p]),
+    "si_scores_topk_mask": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_size_t, c_void_p]),
     "si_csa_build_idx": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "si_csa_build_idx_ex": (c_int, [c_void_p, c_int, c_int, ctypes.c_longlong, c_int, c_int, c_int, c_void_p,
                                     c_void_p]),
     "si_hca_build_idx": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "si_token_compressor": (c_int, [c_void_p] * 6 + [c_int] * 6 + [c_void_p, c_void_p]),
     "si_mean_pool": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "si_indexer_score": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -44,21 +44,54 @@ def csa_index_list(comp_idx: torch.Tensor, n_win: int) -> torch.Tensor:
     return out
 
 
-def scores_topk(scores: torch.Tensor, top_k: int, causal_ratio: Optional[int] = None):
-    """Top-k (score desc, index asc) of materialised scores ``[B,S,T]`` under ``t < (s+1)//causal_ratio``."""
+def scores_topk(scores: torch.Tensor, top_k: int, causal_ratio: Optional[int] = None,
+                causal_mask: Optional[torch.Tensor] = None):
+    """Top-k (score desc, index asc) of materialised scores ``[B,S,T]`` under
+    ``t < (s+1)//causal_ratio`` and/or an explicit bool mask (True = legal)."""
     assert scores.is_cuda and scores.dim() == 3
     B, S, T = scores.shape
     sc = scores.float().contiguous()
     dev = sc.device
+    m = None
+    if causal_mask is not None:
+        m = causal_mask.to(device=dev, dtype=torch.bool).expand(B, S, T).contiguous().view(torch.uint8)
     out_i = torch.empty((B, S, top_k), dtype=torch.int64, device=dev)
     out_v = torch.empty((B, S, top_k), dtype=torch.float32, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
         wsb = lib.si_scores_topk_ws_bytes(B, S, top_k)
         ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        _lib.check(lib.si_scores_topk(sc.data_ptr(), B, S, T, int(top_k), int(causal_ratio or 0), out_i.data_ptr(),
-                                      out_v.data_ptr(), ws.data_ptr(), wsb, _lib.stream_handle(dev)))
+        _lib.check(lib.si_scores_topk_mask(sc.data_ptr(), B, S, T, int(top_k), int(causal_ratio or 0), _lib.ptr(m),
+                                           out_i.data_ptr(), out_v.data_ptr(), ws.data_ptr(), wsb,
+                                           _lib.stream_handle(dev)))
     return out_i, out_v
+
+
+def token_compressor(c_a, z_a, b_a, m: int, *, c_b=None, z_b=None, b_b=None, overlap: bool = False):
+    """Softmax-gated compressor ``[B,S,c] -> [B,S//m,c]`` (``reference_token_compressor``,
+    ``flash_sparse/reference.py:176-272``); bf16 or fp32 tensors, fp32 math."""
+    assert c_a.is_cuda and c_a.dim() == 3 and z_a.shape == c_a.shape
+    B, S, c = c_a.shape
+    if b_a.shape != (m, c):
+        raise ValueError(f"b_a must be [m={m}, c={c}], got {tuple(b_a.shape)}")
+    if overlap:
+        if c_b is None or z_b is None or b_b is None:
+            raise ValueError("overlap=True requires c_b, z_b, b_b")
+        if b_b.shape != (m, c):
+            raise ValueError(f"b_b must be [m={m}, c={c}], got {tuple(b_b.shape)}")
+    dt = c_a.dtype
+    if dt not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"compressor supports bf16 and fp32 tensors, got {dt}")
+    cv = lambda t: None if t is None else t.to(device=c_a.device, dtype=dt).contiguous()  # noqa: E731
+    ca, za, ba, cb, zb, bb = cv(c_a), cv(z_a), cv(b_a), cv(c_b), cv(z_b), cv(b_b)
+    out = torch.empty((B, S // m, c), dtype=dt, device=c_a.device)
+    lib = _lib.load()
+    with torch.cuda.device(c_a.device):
+        _lib.check(lib.si_token_compressor(ca.data_ptr(), za.data_ptr(), ba.data_ptr(), _lib.ptr(cb), _lib.ptr(zb),
+                                           _lib.ptr(bb), B, S, c, int(m), int(bool(overlap)),
+                                           int(dt == torch.bfloat16), out.data_ptr(),
+                                           _lib.stream_handle(c_a.device)))
+    return out
 
 
 def build_csa_topk_idxs(

@@ -140,3 +140,87 @@ int si_hca_build_idx(int B, int S, int n_win, int n_comp, int m_prime, int32_t* 
 }
 
 }  // extern "C"
+
+namespace si {
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Softmax-gated token compressor (flash_sparse/reference.py:176-272), one
+// thread per (b, block, channel), fp32 math.  Non-overlapping: weights =
+// softmax over the block's m tokens of z_a + b_a.  Overlapping: a joint 2m-way
+// softmax over the block's a-stream (z_a + b_a, values c_a) and the previous
+// block's b-stream (z_b + b_b, values c_b; absent for block 0).
+template <typename T>
+__global__ void token_compressor_kernel(const T* __restrict__ ca, const T* __restrict__ za,
+                                        const T* __restrict__ ba, const T* __restrict__ cb,
+                                        const T* __restrict__ zb, const T* __restrict__ bb, int B, int S, int C,
+                                        int m, int overlap, T* __restrict__ out) {
+  const int nb = S / m;
+  const long long total = (long long)B * nb * C;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const long long bn = i / C;
+    const int n = (int)(bn % nb);
+    const int b = (int)(bn / nb);
+    const long long row0 = (long long)b * S + (long long)n * m;  // first token of block n
+    const bool use_b = overlap && n > 0;
+    float mx = -INFINITY;
+    for (int j = 0; j < m; ++j) mx = fmaxf(mx, to_f(za[(row0 + j) * C + c]) + to_f(ba[j * C + c]));
+    if (use_b)
+      for (int j = 0; j < m; ++j) mx = fmaxf(mx, to_f(zb[(row0 - m + j) * C + c]) + to_f(bb[j * C + c]));
+    float den = 0.f, num = 0.f;
+    for (int j = 0; j < m; ++j) {
+      const float e = __expf(to_f(za[(row0 + j) * C + c]) + to_f(ba[j * C + c]) - mx);
+      den += e;
+      num += e * to_f(ca[(row0 + j) * C + c]);
+    }
+    if (use_b)
+      for (int j = 0; j < m; ++j) {
+        const float e = __expf(to_f(zb[(row0 - m + j) * C + c]) + to_f(bb[j * C + c]) - mx);
+        den += e;
+        num += e * to_f(cb[(row0 - m + j) * C + c]);
+      }
+    out[i] = from_f<T>(num / den);
+  }
+}
+
+}  // namespace si
+
+extern "C" {
+
+int si_token_compressor(const void* c_a, const void* z_a, const void* b_a, const void* c_b, const void* z_b,
+                        const void* b_b, int B, int S, int C, int m, int overlap, int is_bf16, void* out,
+                        cudaStream_t stream) {
+  if (B < 1 || S < 0 || C < 1 || m < 1) return si::fail("token_compressor: bad sizes");
+  if (!c_a || !z_a || !b_a || !out) return si::fail("token_compressor: null pointer");
+  if (overlap && (!c_b || !z_b || !b_b)) return si::fail("token_compressor: overlap needs c_b, z_b, b_b");
+  const long long n = (long long)B * (S / m) * C;
+  if (n == 0) return 0;
+  const int grid = si::elementwise_grid(n);
+  if (is_bf16) {
+    using T = __nv_bfloat16;
+    si::token_compressor_kernel<T><<<grid, 256, 0, stream>>>(
+        (const T*)c_a, (const T*)z_a, (const T*)b_a, (const T*)c_b, (const T*)z_b, (const T*)b_b, B, S, C, m,
+        overlap, (T*)out);
+  } else {
+    si::token_compressor_kernel<float><<<grid, 256, 0, stream>>>(
+        (const float*)c_a, (const float*)z_a, (const float*)b_a, (const float*)c_b, (const float*)z_b,
+        (const float*)b_b, B, S, C, m, overlap, (float*)out);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : si::fail_cuda("token_compressor: launch", e);
+}
+
+}  // extern "C"

@@ -1082,7 +1082,7 @@ constexpr int kRowWarps = 8;
 
 __global__ void __launch_bounds__(32 * kRowWarps)
     scores_topk_kernel(const float* __restrict__ scores, int B, int S, int T, int ksel, int ratio, int cap,
-                       unsigned long long* cand, unsigned long long* out_keys) {
+                       const uint8_t* __restrict__ mask, unsigned long long* cand, unsigned long long* out_keys) {
   __shared__ uint32_t hist[kRowWarps][256];
   const int wl = threadIdx.x / 32;
   const uint32_t lane = lane_id();
@@ -1106,8 +1106,9 @@ __global__ void __launch_bounds__(32 * kRowWarps)
         cnt = ksel;
       }
       const int t = t0 + (int)lane;
-      const unsigned long long key = t < lim ? make_key(sr[t], t) : 0ull;
-      const bool pass = t < lim && key > thr;
+      const bool legal = t < lim && (!mask || mask[row * (long long)T + t] != 0);
+      const unsigned long long key = legal ? make_key(sr[t], t) : 0ull;
+      const bool pass = legal && key > thr;
       const uint32_t bal = __ballot_sync(0xffffffffu, pass);
       if (pass) buf[cnt + __popc(bal & lt)] = key;
       cnt += __popc(bal);
@@ -1139,8 +1140,9 @@ size_t si_scores_topk_ws_bytes(int B, int S, int top_k) {
                                 sizeof(unsigned long long);
 }
 
-int si_scores_topk(const float* scores, int B, int S, int T, int top_k, int causal_ratio, int64_t* out_idx,
-                   float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream) {
+int si_scores_topk_mask(const float* scores, int B, int S, int T, int top_k, int causal_ratio,
+                        const uint8_t* causal_mask, int64_t* out_idx, float* out_scores, void* ws, size_t ws_bytes,
+                        cudaStream_t stream) {
   if (top_k < 1 || top_k > 2048) return si::fail("scores_topk: top_k must be in [1, 2048] (got %d)", top_k);
   if (B < 1 || S < 0 || T < 0) return si::fail("scores_topk: bad sizes");
   if ((S > 0 && T > 0 && !scores) || !out_idx || !out_scores || !ws) return si::fail("scores_topk: null pointer");
@@ -1155,12 +1157,18 @@ int si_scores_topk(const float* scores, int B, int S, int T, int top_k, int caus
   const int grid = si::scores_topk_grid(rows);
   auto* keys = reinterpret_cast<unsigned long long*>(out_idx);
   si::scores_topk_kernel<<<grid, 32 * si::kRowWarps, 0, stream>>>(
-      scores, B, S, T, top_k, causal_ratio > 0 ? causal_ratio : 0, si::pick_cap(top_k),
+      scores, B, S, T, top_k, causal_ratio > 0 ? causal_ratio : 0, si::pick_cap(top_k), causal_mask,
       reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(ws) + si::kStatusBytes), keys);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return si::fail_cuda("scores_topk: launch", e);
   e = si::launch_row_sort(keys, out_scores, rows, top_k, stream);
   return e == cudaSuccess ? 0 : si::fail_cuda("scores_topk: row sort", e);
+}
+
+int si_scores_topk(const float* scores, int B, int S, int T, int top_k, int causal_ratio, int64_t* out_idx,
+                   float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  return si_scores_topk_mask(scores, B, S, T, top_k, causal_ratio, nullptr, out_idx, out_scores, ws, ws_bytes,
+                             stream);
 }
 
 }  // extern "C"

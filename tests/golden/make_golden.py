@@ -131,6 +131,15 @@ def main():
     oh = plain(R.reference_hca_forward(fx(qh.float()), fx(kvh.float()), fx(kvc.float()), fx(sinkh), nw, m_prime=mp))
     out["hca"] = dict(q=qh, kv=kvh, kv_c=kvc, sink=sinkh, n_win=nw, m_prime=mp, o=oh.float())
 
+    # 5. general softmax-gated compressor, non-overlapping mode (the overlapping
+    #    mode's body is unreachable in the shipped reference)
+    g3 = torch.Generator("cpu").manual_seed(19)
+    cx = torch.randn((2, 37, 24), generator=g3)
+    zx = torch.randn((2, 37, 24), generator=g3)
+    bx = torch.randn((8, 24), generator=g3)
+    comp8 = plain(R.reference_token_compressor(fx(cx), fx(zx), fx(bx), 8, overlap=False))
+    out["compress_gated"] = dict(c=cx, z=zx, b=bx, m=8, out=comp8)
+
     only = os.environ.get("GOLDEN_ONLY")
     for name, d in out.items():
         if only and name not in only.split(","):

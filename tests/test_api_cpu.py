@@ -9,6 +9,7 @@ import torch
 def test_flash_sparse_import_paths():
     from flash_sparse.csa import build_csa_topk_idxs, flash_csa_forward  # noqa: F401
     from flash_sparse.hca import build_hca_topk_idxs, flash_hca_forward  # noqa: F401
+    from flash_sparse.reference import reference_csa_forward, reference_token_compressor  # noqa: F401
     from flash_sparse.triton import sparse_attn, sparse_attn_bwd, sparse_attn_fwd  # noqa: F401
     from flash_sparse.triton.chunked_indexer import chunked_indexer_topk  # noqa: F401
     from flash_sparse.triton.indexer_score import indexer_score, indexer_score_topk  # noqa: F401

@@ -123,3 +123,50 @@ def test_csa_forward_slices_equal_whole_sequence():
                                top_k=k, m=m, d_v=512) for a, b in zip(bounds, bounds[1:])]
     torch.cuda.synchronize()
     assert torch.equal(torch.cat(parts, dim=1), full)
+
+
+def test_gated_compressor_golden_and_overlap(golden):
+    from streamindex_b200.csa import token_compressor
+
+    d = golden("compress_gated")
+    got = token_compressor(d["c"].cuda(), d["z"].cuda(), d["b"].cuda(), d["m"]).cpu()
+    torch.testing.assert_close(got, d["out"], rtol=1e-4, atol=1e-5)
+    g = torch.Generator().manual_seed(23)
+    B, S, C, m = 2, 42, 40, 4
+    ca, za, cb, zb = (torch.randn((B, S, C), generator=g) for _ in range(4))
+    ba, bb = torch.randn((m, C), generator=g), torch.randn((m, C), generator=g)
+    got = token_compressor(ca.bfloat16().cuda(), za.bfloat16().cuda(), ba.bfloat16().cuda(), m,
+                           c_b=cb.bfloat16().cuda(), z_b=zb.bfloat16().cuda(), b_b=bb.bfloat16().cuda(),
+                           overlap=True).float().cpu()
+    ref = oracle.token_compressor(ca.bfloat16(), za.bfloat16(), ba.bfloat16(), m, cb.bfloat16(), zb.bfloat16(),
+                                  bb.bfloat16(), overlap=True).float()
+    assert (got - ref).abs().max().item() <= 2e-2
+
+
+def test_flash_sparse_reference_module(golden):
+    import flash_sparse.reference as R
+
+    d = golden("idx_v4")
+    sc = R.reference_lightning_indexer(d["q"].cuda(), d["k"].cuda(), d["w"].cuda()).cpu()
+    assert oracle.score_close(sc, d["scores"], 1e-2)
+    d = golden("attn_128")
+    o = R.reference_sparse_attn(d["q"].cuda(), d["kv"].cuda(), d["sink"].cuda(), d["idx"].cuda())
+    assert (o.float().cpu() - d["o"]).abs().max().item() <= 2e-2
+    d = golden("hca")
+    o = R.reference_hca_forward(d["q"].cuda(), d["kv"].cuda(), d["kv_c"].cuda(), d["sink"].cuda(), d["n_win"],
+                                m_prime=d["m_prime"])
+    assert (o.float().cpu() - d["o"]).abs().max().item() <= 2e-2
+    # CSA with an explicit compressed mask vs the oracle's index build
+    g = torch.Generator().manual_seed(29)
+    B, S, H, D, T, nw, k = 1, 40, 8, 64, 10, 4, 6
+    q = (torch.randn((B, S, H, D), generator=g) * D ** -0.5).bfloat16()
+    kv = torch.randn((B, S, D), generator=g).bfloat16()
+    kvc = torch.randn((B, T, D), generator=g).bfloat16()
+    scores = torch.randn((B, S, T), generator=g)
+    legal = (torch.arange(S).view(1, -1, 1) >= (torch.arange(T) + 1).view(1, 1, -1) * 4 - 1)
+    sink = torch.randn(H, generator=g)
+    o = R.reference_csa_forward(q.cuda(), kv.cuda(), kvc.cuda(), scores.cuda(), sink.cuda(), nw, k,
+                                causal_mask_for_compressed=legal.cuda()).float().cpu()
+    idx = oracle.build_csa_topk_idxs(scores, nw, k, 4)
+    ro, _ = oracle.sparse_attn(q, torch.cat([kv, kvc], dim=1), sink, idx)
+    assert (o - ro).abs().max().item() <= 2e-2

@@ -70,3 +70,13 @@ def test_hca_forward_matches_reference(golden):
                                    d["m_prime"])
     torch.testing.assert_close(o, d["o"], rtol=1e-5, atol=1e-5)
     assert idx.dtype == torch.int32
+
+
+def test_gated_compressor_matches_reference(golden):
+    d = golden("compress_gated")
+    got = oracle.token_compressor(d["c"], d["z"], d["b"], d["m"])
+    torch.testing.assert_close(got, d["out"], rtol=1e-5, atol=1e-5)
+    # zero scores and bias reduce it to the mean pool
+    z0 = torch.zeros_like(d["z"])
+    torch.testing.assert_close(oracle.token_compressor(d["c"], z0, torch.zeros_like(d["b"]), d["m"]),
+                               oracle.mean_pool_compress(d["c"], d["m"]), rtol=1e-6, atol=1e-6)
