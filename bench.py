@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-queries", type=int, default=96)
     ap.add_argument("--no-gather", action="store_true")
+    ap.add_argument("--attn-heads", type=int, default=64, help="attention workload: query heads (64; 128 = V4-Pro)")
+    ap.add_argument("--attn-k", type=int, default=512, help="attention workload: selected kv rows per query")
     ap.add_argument("--workload", default="indexer", choices=["indexer", "attn", "csa"],
                     help="indexer: the headline metric (default); attn: BASELINE configs[3] sparse attention")
     return ap.parse_args()
@@ -423,7 +425,7 @@ def run_attn(a):
     """sparse attention forward, B=1, S=65536, H=64, D=576/512, N_kv=16384, K=512."""
     from streamindex_b200 import _lib
 
-    S, H, D, DV, NKV, K = a.S, 64, 576, 512, 16384, 512
+    S, H, D, DV, NKV, K = a.S, a.attn_heads, 576, 512, 16384, a.attn_k
     device = torch.device("cuda", 0)
     g = torch.Generator(device=device)
     g.manual_seed(0)
@@ -478,7 +480,7 @@ def run_attn(a):
         "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; causal uniform indices without replacement)",
-        "config": {"workload": "sparse_attn_fwd B=1 S=%d H=64 D_qk=576 D_v=512 N_kv=16384 K=512" % S,
+        "config": {"workload": "sparse_attn_fwd B=1 S=%d H=%d D_qk=576 D_v=512 N_kv=16384 K=%d" % (S, H, K),
                    "valid_slots": V, "l2": "q/o larger than L2; kv (18.9 MB) L2-resident by design"},
         "gpu_launches": a.steps,
         "roofline": {"bound": "tensor", "achieved": tf, "peak": tf_peak, "unit": "TFLOP/s", "frac": tf / tf_peak,
