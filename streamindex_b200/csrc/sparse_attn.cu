@@ -17,19 +17,23 @@
 // O lives there (lanes 0-15, columns [0,Dv)) and the two S buffers live in
 // lanes 16-31 (columns [0,2*NK)), so the whole TMEM is used without overlap.
 //
-// Softmax warps (4, one per lane quarter = 16 heads): thread 16+i of a warp
-// owns head row i of S and computes the online softmax for it; thread i owns
-// the same head's O row.  The running shift is only raised when the tile max
+// Softmax warps (4, one per lane quarter = 16 heads): threads i and 16+i of a
+// warp share head row i, each taking 16 of the tile's 32 scores (16x32bx2 TMEM
+// load from the S lanes) and half of the row's O columns; row max and sum are
+// combined with one shuffle.  The running shift is only raised when the tile max
 // exceeds it by more than 8 (log2 units), so O is rescaled (ld/scale/st with
 // the 16x32bx2 TMEM shape, which touches lanes 0-15 only) rarely; P = exp2(s -
 // shift) <= 256 stays well inside the bf16 range.  P goes to shared memory (bf16) as
 // the A operand of MMA2.
 //
-// Warp roles (480 threads): warp 0 TMA for the Q tile, warp 1 TMEM alloc +
-// UMMA issue, warps 2-5 softmax / O correction / output, warps 6-13 kv row
-// gathers with 16-byte cp.async (completion signalled on the stage barrier with
-// cp.async.mbarrier.arrive.noinc), warp 14 TMA gather4 for the first atoms of
-// each row (single kv tensor only).
+// Warp roles (544 threads): warp 0 TMA for the Q tile (and an L2 prefetch of
+// the next item's Q), warp 1 TMEM alloc + Q.K^T issue, warp 16 P.V issue, warps 2-5 softmax / O
+// correction / output, warps 6-13 kv row gathers with 16-byte cp.async
+// (completion signalled on the stage barrier with cp.async.mbarrier.arrive.noinc),
+// warp 14 TMA gather4 for the first atoms of each row (single kv tensor only) and
+// the per-stage valid-slot mask, warp 15 the index ring: it reads the selected
+// indices several tiles ahead into shared memory, so no gather thread waits on a
+// global load of an index.
 #include <cuda_bf16.h>
 
 #include "capi_common.h"
@@ -40,9 +44,11 @@ namespace si {
 namespace attn {
 
 constexpr int kHeads = 64;    // UMMA M (heads per work item)
-constexpr int kThreads = 480;   // + warp 14: TMA row gathers
+constexpr int kThreads = 544;   // + warp 14: TMA row gathers, warp 15: index ring, warp 16: P.V issue
+constexpr int kIdxSlots = 8;    // index-ring slots (one tile of NK indices each)
 constexpr int kGatherWarps = 8;   // warps 6-13
 constexpr int kSmemMax = 232448;
+constexpr int kMaxAtoms = 16;  // D <= 1024
 
 struct Params {
   int B, S, H, D;      // D: qk head dim (multiple of 8)
@@ -72,7 +78,14 @@ struct Params {
     if (p.trace && blockIdx.x == 0 && (item) < 4 && (tile) < 16)                                        \
       p.trace[(((role) * 4 + (item)) * 16 + (tile)) * 8 + (pt)] = globaltimer();                         \
   } while (0)
+#define SI_TRACE_IF(cond, role, item, tile, pt) \
+  do {                                          \
+    if (cond) SI_TRACE(role, item, tile, pt);   \
+  } while (0)
 #else
+#define SI_TRACE_IF(cond, role, item, tile, pt) \
+  do {                                          \
+  } while (0)
 #define SI_TRACE(role, item, tile, pt) \
   do {                                 \
   } while (0)
@@ -80,6 +93,9 @@ struct Params {
 
 struct __align__(8) Misc {
   uint64_t kv_full[8], kv_empty[8];
+  uint64_t idx_full[kIdxSlots], idx_empty[kIdxSlots];
+  uint32_t kvmask[8];             // valid-slot mask of the tile in each kv stage
+  int idx_ring[kIdxSlots][32];    // selected kv rows of upcoming tiles (-1 = masked)
   uint64_t q_full, q_empty;
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
@@ -110,17 +126,6 @@ __host__ __device__ inline size_t smem_bytes(int NA) {
 namespace si {
 namespace attn {
 
-// Index of a kv row for the gather, or an out-of-range row (zero-filled by
-// TMA) when the slot is masked (-1) or past the end of the index list.
-// Selected kv index of slot kk of query (b, s), and whether it is a legal row
-// (-1 and indices >= Nkv are masked; slots past K are padding).
-__device__ __forceinline__ int gather_row(const Params& p, int b, int s, int kk, bool& valid) {
-  int v = -1;
-  if (kk < p.K) v = p.idx[((size_t)b * p.S + s) * p.K + kk];
-  valid = v >= 0 && v < p.Nkv;
-  return valid ? v : 0;
-}
-
 // Address of kv row v of batch b in the (possibly split) kv storage.
 __device__ __forceinline__ const __nv_bfloat16* kv_row_ptr(const Params& p, int b, int v) {
   if (v < p.Nkv1) return p.kv + ((size_t)b * p.Nkv1 + v) * p.D;
@@ -134,11 +139,15 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
   constexpr float kLog2e = 1.4426950408889634f;
   const int qd = warp & 3;
   const int r = (int)(lane & 15);          // row within the quarter
-  const bool srow = lane >= 16;            // this lane holds an S row
+  const int half = (int)(lane >> 4);       // which 16 of the tile's 32 keys / which half of O's columns
   const int hrow = 16 * qd + r;            // row within the 64-head group
   const uint32_t tq = tmem + ((uint32_t)(32 * qd) << 16);
   volatile int* abort_flag = &ms->abort_flag;
   uint32_t sf[2] = {0, 0};
+  // kv stage of the current tile (same ring walk as the gather and MMA roles):
+  // its valid-slot mask is published before the stage's kv_full arrival
+  const uint32_t nst = (uint32_t)num_stages<NK>(p.NA);
+  uint32_t kst = 0, kph = 0;
   // MMA2 of tile j signals pv_done[j & 1]; waited[b] counts completions of
   // barrier b already consumed, so "MMA2 of tile j is done" is a wait for
   // completion number (j >> 1) of barrier j & 1 (skipped if already seen).
@@ -156,39 +165,50 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
   for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
     const int hg = it % p.hgroups;
     const int bs = it / p.hgroups;
-    const int b = bs / p.S, s = bs % p.S;
     const int head = hg * kHeads + hrow;
+#ifdef SI_ATTN_TRACE
     const int ii = (it - (int)blockIdx.x) / (int)gridDim.x;
-    const bool tr = (warp == 2 && lane == 16);
+    const bool tr = (warp == 2 && lane == 0);
+#endif
     const float sink2 = head < p.H ? p.sink[head] * kLog2e : 0.f;
+    // m_used / l are kept identically by both half-warp threads of a row
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    bool valid_next;
-    gather_row(p, b, s, (int)lane, valid_next);
     for (int t = 0; t < ntiles; ++t) {
-      const uint32_t vmask = __ballot_sync(0xffffffffu, valid_next);
-      if (t + 1 < ntiles) gather_row(p, b, s, (t + 1) * NK + (int)lane, valid_next);  // prefetch
-      if (tr) SI_TRACE(2, ii, t, 0);
+      SI_TRACE_IF(tr, 2, ii, t, 0);
       if (!mbar_wait(&ms->s_full[t & 1], sf[t & 1], abort_flag, p.status, kErrWaitAccFull)) {
         ok = false;
         break;
       }
       sf[t & 1] ^= 1;
+      // S of this tile is complete, so its kv stage has long been filled; the
+      // wait only acquires the mask written before the stage's arrival
+      if (!mbar_wait(&ms->kv_full[kst], kph, abort_flag, p.status, kErrWaitTmaFull)) {
+        ok = false;
+        break;
+      }
+      const uint32_t vmask = *reinterpret_cast<volatile uint32_t*>(&ms->kvmask[kst]) >> (half * 16);
+      if (++kst == nst) {
+        kst = 0;
+        kph ^= 1;
+      }
       tc_fence_after();
-      float sv[NK];
-      if (tr) SI_TRACE(2, ii, t, 1);
-      tmem_ld32_sync(tq + (t & 1) * NK, sv);
-      if (tr) SI_TRACE(2, ii, t, 2);
+      SI_TRACE_IF(tr, 2, ii, t, 1);
+      float sv[16];
+      tmem_ld16x32bx2_x16_sync<16>(tq + (16u << 16) + (t & 1) * NK, sv);
+      SI_TRACE_IF(tr, 2, ii, t, 2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ms->s_free[t & 1]);
 
-      float mt = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int j = 0; j < NK; ++j) {
+      for (int j = 0; j < 16; ++j) {
         sv[j] = ((vmask >> j) & 1u) ? sv[j] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, sv[j]);
+        mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
       }
+      float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
       bool rescale = false;
       float alpha = 1.f;
       if (mt > -INFINITY) {
@@ -201,19 +221,22 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
           rescale = true;
         }
       }
-      float psum = 0.f;
       // m_used = -inf only while no valid key has been seen; then every p is 0
       const float shift = (m_used == -INFINITY) ? INFINITY : m_used;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < NK; ++j) {
+      for (int j = 0; j < 16; ++j) {
         sv[j] = ex2_approx(sv[j] - shift);
-        psum += sv[j];
+        ps[j & 3] += sv[j];
       }
+      float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      psum += __shfl_xor_sync(0xffffffffu, psum, 16);
       l += psum;
+      SI_TRACE_IF(tr, 2, ii, t, 5);
 
       // P buffer t&1 was last read by MMA2 of tile t-2; a rescale of O also
       // needs MMA2 of tile t-1 to be complete.
-      const bool any_rescale = __any_sync(0xffffffffu, rescale && srow);
+      const bool any_rescale = __any_sync(0xffffffffu, rescale);
       if (t >= 2 && !wait_pv(t - 2)) {
         ok = false;
         break;
@@ -223,23 +246,23 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
         break;
       }
       tc_fence_after();
-      if (tr) SI_TRACE(2, ii, t, 3);
+      SI_TRACE_IF(tr, 2, ii, t, 3);
       if (any_rescale) {
-        const float a_row = __shfl_sync(0xffffffffu, srow ? alpha : 1.f, 16 + r);
 #pragma unroll 1
         for (int c = 0; c < DVH / 32; ++c) {
           float v[32];
           tmem_ld16x32bx2_x32_sync<DVH>(tq + c * 32, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= a_row;
+          for (int j = 0; j < 32; ++j) v[j] *= alpha;
           tmem_st16x32bx2_x32<DVH>(tq + c * 32, v);
         }
         tmem_st_wait();
       }
-      if (srow) {
-        uint8_t* prow = sP + (t & 1) * NK * 128 + (hrow >> 3) * 128 + (hrow & 7) * 16;
+      {
+        // P row hrow, keys [16*half, 16*half+16): two 8-key core-matrix chunks
+        uint8_t* prow = sP + (t & 1) * NK * 128 + (hrow >> 3) * 128 + (hrow & 7) * 16 + half * 2048;
 #pragma unroll
-        for (int kc = 0; kc < NK / 8; ++kc) {
+        for (int kc = 0; kc < 2; ++kc) {
           uint4 u;
           u.x = pack_bf16x2(sv[kc * 8 + 0], sv[kc * 8 + 1]);
           u.y = pack_bf16x2(sv[kc * 8 + 2], sv[kc * 8 + 3]);
@@ -252,7 +275,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ms->p_full[t & 1]);
-      if (tr) SI_TRACE(2, ii, t, 4);
+      SI_TRACE_IF(tr, 2, ii, t, 4);
     }
     if (!ok) break;
     if ((ntiles >= 2 && !wait_pv(ntiles - 2)) || !wait_pv(ntiles - 1)) break;
@@ -264,10 +287,9 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
     if (m_used == -INFINITY) m_used = sink2;  // no valid key: O = 0, l = exp(sink - sink)
     const float l_tot = l + exp2f(sink2 - m_used);
     const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-    if (srow && head < p.H && p.lse)
+    if (half == 0 && head < p.H && p.lse)
       p.lse[(size_t)bs * p.H + head] = l_tot > 0.f ? (m_used + log2f(l_tot)) * kLn2 : -1.0e30f;
-    const float inv_row = __shfl_sync(0xffffffffu, inv, 16 + r);
-    __nv_bfloat16* orow = p.o + ((size_t)bs * p.H + head) * p.o_ld + p.o_off + (lane >> 4) * DVH;
+    __nv_bfloat16* orow = p.o + ((size_t)bs * p.H + head) * p.o_ld + p.o_off + half * DVH;
 #pragma unroll 1
     for (int c = 0; c < DVH / 32; ++c) {
       float v[32];
@@ -276,10 +298,10 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {
           uint4 u;
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j + 0] * inv_row, v[j + 1] * inv_row);
-          __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2] * inv_row, v[j + 3] * inv_row);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4] * inv_row, v[j + 5] * inv_row);
-          __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6] * inv_row, v[j + 7] * inv_row);
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j + 0] * inv, v[j + 1] * inv);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2] * inv, v[j + 3] * inv);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4] * inv, v[j + 5] * inv);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6] * inv, v[j + 7] * inv);
           u.x = *reinterpret_cast<uint32_t*>(&h0);
           u.y = *reinterpret_cast<uint32_t*>(&h1);
           u.z = *reinterpret_cast<uint32_t*>(&h2);
@@ -320,9 +342,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NST; ++i) {
-      // one cp.async completion arrival per gather thread (+ the TMA warp's expect_tx arrival)
-      mbar_init(&ms->kv_full[i], kGatherWarps * 32 + (p.na_tma > 0 ? 1 : 0));
+      // one cp.async completion arrival per gather thread + the TMA warp's
+      // arrival (with its byte count when it gathers atoms)
+      mbar_init(&ms->kv_full[i], kGatherWarps * 32 + 1);
       mbar_init(&ms->kv_empty[i], 1);
+    }
+    for (int i = 0; i < kIdxSlots; ++i) {
+      mbar_init(&ms->idx_full[i], 32);                // every lane of the index warp
+      mbar_init(&ms->idx_empty[i], kGatherWarps + 1);  // gather warps + TMA warp
     }
     mbar_init(&ms->q_full, 1);
     mbar_init(&ms->q_empty, 1);
@@ -356,6 +383,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
       const int hg = it % p.hgroups;
       const int bs = it / p.hgroups;
+      const int nx = it + (int)gridDim.x;
+      if (nx < nitems && lane < NA) {  // next item's Q into L2 while this one runs
+        const int nrow = (nx / p.hgroups) * p.H + (nx % p.hgroups) * kHeads;
+        tma_prefetch_l2_2d(&map_q, (int)lane * 64, nrow);
+      }
       if (!mbar_wait(&ms->q_empty, qph ^ 1, abort_flag, p.status, kErrWaitQ)) break;
       qph ^= 1;
       if (lane == 0) {
@@ -367,25 +399,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 6 + kGatherWarps) {
     // ------------------------------------------------------------ TMA row gathers (gather4) of atoms [0, na_tma)
-    if (p.na_tma > 0) {
-      uint32_t st = 0, kph = 0;
-      const int g4 = (int)lane & 7;
-      const int a = (int)lane >> 3;
-      for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
-        const int bs = it / p.hgroups;
-        const int b = bs / p.S, s = bs % p.S;
-        bool valid_next;
-        int row_next = gather_row(p, b, s, (int)lane, valid_next);
-        bool ok = true;
-        for (int t = 0; t < ntiles; ++t) {
-          const int row = valid_next ? b * p.Nkv + row_next : p.B * p.Nkv;  // out of range: zero fill
-          if (t + 1 < ntiles) row_next = gather_row(p, b, s, (t + 1) * NK + (int)lane, valid_next);
-          if (!mbar_wait(&ms->kv_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
-            ok = false;
-            break;
-          }
-          if (lane == 0) mbar_expect_tx(&ms->kv_full[st], (uint32_t)(p.na_tma * NK * 128));
-          __syncwarp();
+    // and the valid-slot mask of every tile (published before this warp's kv_full arrival)
+    uint32_t st = 0, kph = 0, islot = 0, iph = 0;
+    const int g4 = (int)lane & 7;
+    const int a = (int)lane >> 3;
+    bool ok = true;
+    for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      const int bs = it / p.hgroups;
+      const int b = bs / p.S;
+      for (int t = 0; t < ntiles; ++t) {
+        if (!mbar_wait(&ms->idx_full[islot], iph, abort_flag, p.status, kErrWaitTmaFull)) {
+          ok = false;
+          break;
+        }
+        const int v = ms->idx_ring[islot][lane];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ms->idx_empty[islot]);
+        if (++islot == (uint32_t)kIdxSlots) {
+          islot = 0;
+          iph ^= 1;
+        }
+        const uint32_t vm = __ballot_sync(0xffffffffu, v >= 0);
+        const int row = v >= 0 ? b * p.Nkv + v : p.B * p.Nkv;  // out of range: zero fill
+        if (!mbar_wait(&ms->kv_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          ms->kvmask[st] = vm;
+          if (p.na_tma > 0)
+            mbar_expect_tx(&ms->kv_full[st], (uint32_t)(p.na_tma * NK * 128));
+          else
+            mbar_arrive(&ms->kv_full[st]);
+        }
+        __syncwarp();
+        if (p.na_tma > 0) {
           const int r0 = __shfl_sync(0xffffffffu, row, 4 * g4 + 0);
           const int r1 = __shfl_sync(0xffffffffu, row, 4 * g4 + 1);
           const int r2 = __shfl_sync(0xffffffffu, row, 4 * g4 + 2);
@@ -394,57 +442,98 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_gather4(sKV + (size_t)st * SB + a * NK * 128 + g4 * 4 * 128, &map_kv, &ms->kv_full[st], a * 64, r0,
                         r1, r2, r3);
           __syncwarp();
-          if (++st == (uint32_t)NST) {
-            st = 0;
-            kph ^= 1;
-          }
         }
-        if (!ok) break;
+        if (++st == (uint32_t)NST) {
+          st = 0;
+          kph ^= 1;
+        }
       }
     }
-  } else if (warp >= 6) {
-    // ------------------------------------------------------------ KV row gathers (cp.async)
-    // A tile is NK rows x NA 128-byte atoms.  One warp instruction copies 4
-    // atom-rows (8 lanes x 16 B each, a full 128-byte segment of one kv row);
-    // the 4 gather warps interleave the NA*8 instructions of a tile.  The
-    // destination applies the 128-byte swizzle (16-byte chunk c of row r goes
-    // to chunk c ^ (r & 7)), the layout the UMMA descriptors expect.
-    const int gw = warp - 6;
-    uint32_t st = 0, kph = 0;
-    const uint32_t c = lane & 7;
+  } else if (warp == 7 + kGatherWarps) {
+    // ------------------------------------------------------------ index ring producer
+    // Reads the selected indices of 8 tiles at a time (independent loads in
+    // flight together), then publishes them one tile per slot as slots free up.
+    uint32_t islot = 0, iph = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
       const int bs = it / p.hgroups;
       const int b = bs / p.S, s = bs % p.S;
+      const int* src = p.idx + ((size_t)b * p.S + s) * p.K;
+      for (int t0 = 0; t0 < ntiles && ok; t0 += 8) {
+        int v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int kk = (t0 + j) * NK + (int)lane;
+          v[j] = kk < p.K ? src[kk] : -1;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (t0 + j >= ntiles) break;
+          if (!mbar_wait(&ms->idx_empty[islot], iph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
+            ok = false;
+            break;
+          }
+          ms->idx_ring[islot][lane] = (v[j] >= 0 && v[j] < p.Nkv) ? v[j] : -1;
+          mbar_arrive(&ms->idx_full[islot]);
+          if (++islot == (uint32_t)kIdxSlots) {
+            islot = 0;
+            iph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp >= 6 && warp < 6 + kGatherWarps) {
+    // ------------------------------------------------------------ KV row gathers (cp.async)
+    // A tile is NK rows x NA 128-byte atoms.  Gather warp gw owns rows
+    // 4*gw .. 4*gw+3 of every tile: 8 lanes per row, lane & 7 = 16-byte chunk of
+    // an atom, so one warp instruction copies 4 rows x 128 bytes and each thread
+    // computes its row address once per tile and then issues its atoms back to
+    // back.  The destination applies the 128-byte swizzle (16-byte chunk c of row
+    // r goes to chunk c ^ (r & 7)), the layout the UMMA descriptors expect.
+    static_assert(kGatherWarps * 4 == NK, "one gather-warp row quad per 4 tile rows");
+    const int gw = warp - 6;
+    const int r = 4 * gw + (int)(lane >> 3);
+    const uint32_t c = lane & 7;
+    const uint32_t dst_off = (uint32_t)r * 128 + ((c ^ (uint32_t)(r & 7)) << 4);
+    uint32_t st = 0, kph = 0, islot = 0, iph = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      const int bs = it / p.hgroups;
+      const int b = bs / p.S;
+#ifdef SI_ATTN_TRACE
       const int ii = (it - (int)blockIdx.x) / (int)gridDim.x;
       const bool tr = (gw == 0 && lane == 0);
-      bool valid_next;
-      int row_next = gather_row(p, b, s, (int)lane, valid_next);
+#endif
       for (int t = 0; t < ntiles; ++t) {
-        const int row = row_next;
-        const int vld = valid_next ? 1 : 0;
-        if (t + 1 < ntiles) row_next = gather_row(p, b, s, (t + 1) * NK + (int)lane, valid_next);
-        if (tr) SI_TRACE(0, ii, t, 0);
+        SI_TRACE_IF(tr, 0, ii, t, 0);
+        if (!mbar_wait(&ms->idx_full[islot], iph, abort_flag, p.status, kErrWaitTmaFull)) {
+          ok = false;
+          break;
+        }
+        const int row = ms->idx_ring[islot][r];
+        const bool vld = row >= 0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ms->idx_empty[islot]);
+        if (++islot == (uint32_t)kIdxSlots) {
+          islot = 0;
+          iph ^= 1;
+        }
         if (!mbar_wait(&ms->kv_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) {
           ok = false;
           break;
         }
-        if (tr) SI_TRACE(0, ii, t, 1);
-        const uint32_t base = smem_u32(sKV + (size_t)st * SB);
-        for (int q = p.na_tma * 8 + gw; q < NA * 8; q += kGatherWarps) {
-          const int u = q * 4 + (int)(lane >> 3);
-          const int r = u & (NK - 1);
-          const int a = u / NK;
-          const int rv = __shfl_sync(0xffffffffu, row, r);
-          const int vv = __shfl_sync(0xffffffffu, vld, r);
-          const int col = a * 64 + (int)c * 8;
-          const bool in = vv && col < p.D;
-          const __nv_bfloat16* src = in ? kv_row_ptr(p, b, rv) + col : p.kv;
-          cp_async_16(base + a * NK * 128 + r * 128 + ((c ^ (uint32_t)(r & 7)) << 4), src, in ? 16u : 0u);
+        SI_TRACE_IF(tr, 0, ii, t, 1);
+        const uint32_t base = smem_u32(sKV + (size_t)st * SB) + dst_off;
+        const __nv_bfloat16* src = (vld ? kv_row_ptr(p, b, row) : p.kv) + c * 8;
+#pragma unroll
+        for (int a = 0; a < kMaxAtoms; ++a) {
+          if (a >= NA) break;
+          if (a < p.na_tma) continue;
+          const bool in = vld && a * 64 + (int)c * 8 < p.D;
+          cp_async_16(base + a * NK * 128, in ? src + a * 64 : p.kv, in ? 16u : 0u);
         }
         cp_async_arrive_noinc(&ms->kv_full[st]);
-        if (tr) SI_TRACE(0, ii, t, 2);
-        if (tr) SI_TRACE(0, ii, t, 3);
+        SI_TRACE_IF(tr, 0, ii, t, 2);
         if (++st == (uint32_t)NST) {
           st = 0;
           kph ^= 1;
@@ -453,45 +542,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     cp_async_wait<0>();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ UMMA issuer
+    // ------------------------------------------------------------ UMMA issuer: S = Q.K^T
+    // P.V is issued by warp 16, so a P.V never waits behind a Q.K^T whose rows
+    // are still in flight, and (a tcgen05.commit tracks only the issuing
+    // thread's MMAs) an S completion never waits for a P.V.
     if (lane == 0) {
       const uint32_t idesc1 = umma_idesc_f16(kHeads, NK, 1);
-      const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, 1) | (1u << 16);  // B (V) MN-major
-      uint32_t st = 0, kph = 0, qph = 0, pvst = 0;
-      uint32_t sfr[2] = {0, 0}, pf[2] = {0, 0}, ofr = 0;
+      uint32_t st = 0, kph = 0, qph = 0;
+      uint32_t sfr[2] = {0, 0};
       bool ok = true;
-      int ii = 0;
-      auto pv = [&](int j, uint32_t stj) -> bool {
-        if (!mbar_wait(&ms->p_full[j & 1], pf[j & 1], abort_flag, p.status, kErrWaitAccFull)) return false;
-        pf[j & 1] ^= 1;
-        SI_TRACE(1, ii, j, 4);
-        if (j == 0) {
-          if (!mbar_wait(&ms->o_free, ofr ^ 1, abort_flag, p.status, kErrWaitAccEmpty)) return false;
-          ofr ^= 1;
-        }
-        tc_fence_after();
-        const uint32_t pbase = smem_u32(sP + (j & 1) * NK * 128);
-        const uint32_t vbase = smem_u32(sKV + (size_t)stj * SB) + (p.dv_off / 64) * NK * 128;
-#pragma unroll
-        for (int kk = 0; kk < NK / 16; ++kk) {
-          const uint64_t adesc = umma_desc(pbase + kk * 2048, 1024, 128, 0);
-#pragma unroll
-          for (int nh = 0; nh < NCH; ++nh) {
-            const uint64_t bdesc = umma_desc(vbase + nh * (NMMA / 64) * NK * 128 + kk * 2048, NK * 128, 1024, 2);
-            umma_f16(tmem + nh * NMMA, adesc, bdesc, idesc2, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
-        umma_commit(&ms->pv_done[j & 1]);
-        umma_commit(&ms->kv_empty[stj]);
-        SI_TRACE(1, ii, j, 5);
-        return true;
-      };
+      const uint32_t qbase = smem_u32(sQ);
       for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
-        ii = (it - (int)blockIdx.x) / (int)gridDim.x;
+#ifdef SI_ATTN_TRACE
+        const int ii = (it - (int)blockIdx.x) / (int)gridDim.x;
+#endif
         if (!mbar_wait(&ms->q_full, qph, abort_flag, p.status, kErrWaitQ)) break;
         qph ^= 1;
         tc_fence_after();
-        const uint32_t qbase = smem_u32(sQ);
         for (int t = 0; t < ntiles; ++t) {
           SI_TRACE(1, ii, t, 0);
           if (!mbar_wait(&ms->kv_full[st], kph, abort_flag, p.status, kErrWaitTmaFull) ||
@@ -516,17 +583,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&ms->s_full[t & 1]);
           SI_TRACE(1, ii, t, 3);
           if (t == ntiles - 1) umma_commit(&ms->q_empty);
-          if (t >= 1 && !pv(t - 1, pvst)) {
-            ok = false;
-            break;
-          }
-          pvst = st;
           if (++st == (uint32_t)NST) {
             st = 0;
             kph ^= 1;
           }
         }
-        if (!ok || !pv(ntiles - 1, pvst)) break;
+      }
+    }
+  } else if (warp == 8 + kGatherWarps) {
+    // ------------------------------------------------------------ UMMA issuer: O += P.V
+    // Tile j's kv stage is released here: its Q.K^T completed before the
+    // softmax published P, so this commit covers every read of the stage.
+    if (lane == 0) {
+      const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, 1) | (1u << 16);  // B (V) MN-major
+      uint32_t st = 0, pf[2] = {0, 0}, ofr = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+#ifdef SI_ATTN_TRACE
+        const int ii = (it - (int)blockIdx.x) / (int)gridDim.x;
+#endif
+        for (int j = 0; j < ntiles; ++j) {
+          if (!mbar_wait(&ms->p_full[j & 1], pf[j & 1], abort_flag, p.status, kErrWaitAccFull)) {
+            ok = false;
+            break;
+          }
+          pf[j & 1] ^= 1;
+          SI_TRACE(1, ii, j, 4);
+          if (j == 0) {
+            if (!mbar_wait(&ms->o_free, ofr ^ 1, abort_flag, p.status, kErrWaitAccEmpty)) {
+              ok = false;
+              break;
+            }
+            ofr ^= 1;
+          }
+          tc_fence_after();
+          const uint32_t pbase = smem_u32(sP + (j & 1) * NK * 128);
+          const uint32_t vbase = smem_u32(sKV + (size_t)st * SB) + (p.dv_off / 64) * NK * 128;
+#pragma unroll
+          for (int kk = 0; kk < NK / 16; ++kk) {
+            const uint64_t adesc = umma_desc(pbase + kk * 2048, 1024, 128, 0);
+#pragma unroll
+            for (int nh = 0; nh < NCH; ++nh) {
+              const uint64_t bdesc = umma_desc(vbase + nh * (NMMA / 64) * NK * 128 + kk * 2048, NK * 128, 1024, 2);
+              umma_f16(tmem + nh * NMMA, adesc, bdesc, idesc2, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&ms->pv_done[j & 1]);
+          umma_commit(&ms->kv_empty[st]);
+          SI_TRACE(1, ii, j, 5);
+          if (++st == (uint32_t)NST) st = 0;
+        }
       }
     }
   } else {
