@@ -201,14 +201,26 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       __syncwarp();
       if (lane == 0) mbar_arrive(&ms->s_free[t & 1]);
 
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // The max is taken on the raw scores and the scale is folded into the
+      // exponent's FMA (a positive scale keeps the order; any other scale is
+      // applied up front).  Masked slots become -inf, and a fully valid half
+      // tile (the common case) skips the per-slot test.
+      float sc = p.scale_log2;
+      if (!(sc > 0.f)) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        sv[j] = ((vmask >> j) & 1u) ? sv[j] * p.scale_log2 : -INFINITY;
-        mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
+        for (int j = 0; j < 16; ++j) sv[j] *= sc;
+        sc = 1.f;
       }
+      if ((vmask & 0xffffu) != 0xffffu) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (!((vmask >> j) & 1u)) sv[j] = -INFINITY;
+      }
+      float mx[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+      for (int j = 4; j < 16; ++j) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
       float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16)) * sc;
       bool rescale = false;
       float alpha = 1.f;
       if (mt > -INFINITY) {
@@ -226,7 +238,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        sv[j] = ex2_approx(sv[j] - shift);
+        sv[j] = ex2_approx(fmaf(sv[j], sc, -shift));
         ps[j & 3] += sv[j];
       }
       float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
