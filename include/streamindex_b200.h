@@ -110,7 +110,7 @@ SI_API int si_indexer_score(const void* q, const void* k, const void* w, int w_i
 /* Sparse MQA attention forward with attention sink.
  * Replaces sparse_attn_fwd (flash_sparse/triton/sparse_attn_fwd.py:180-292) and
  * the math of reference_sparse_attn (flash_sparse/reference.py:44-130).
- *   q          [B,S,H,D]   bf16        D % 8 == 0
+ *   q          [B,S,H,D]   bf16        D % 8 == 0, D <= 896
  *   kv         [B,Nkv,D]   bf16        one shared KV head
  *   attn_sink  [H]         fp32        enters the softmax denominator only
  *   topk_idxs  [B,S,K]     int32       row of kv per slot; -1 (or >= Nkv) = masked

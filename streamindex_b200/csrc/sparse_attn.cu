@@ -44,11 +44,21 @@ namespace si {
 namespace attn {
 
 constexpr int kHeads = 64;    // UMMA M (heads per work item)
-constexpr int kThreads = 544;   // + warp 14: TMA row gathers, warp 15: index ring, warp 16: P.V issue
+constexpr int kThreads = 672;   // + warp 14: TMA row gathers, 15: index ring, 16: P.V issue, 17-20: Q to TMEM
 constexpr int kIdxSlots = 8;    // index-ring slots (one tile of NK indices each)
 constexpr int kGatherWarps = 8;   // warps 6-13
 constexpr int kSmemMax = 232448;
 constexpr int kMaxAtoms = 16;  // D <= 1024
+constexpr int kQStage = 4;     // Q staging atoms (64 rows x 128 B) in shared memory
+constexpr int kQCol = 64;      // first TMEM column of Q (lanes 16-31 of each quarter), after the two S buffers
+constexpr int kQSlots = (512 - kQCol) / 32;  // 32-column Q atom slots in TMEM (14)
+
+// Q lives in tensor memory as the A operand of Q.K^T.  Its atoms fill a ring
+// of kQSlots 32-column slots: item j's atom a (CTA-local numbering) goes to
+// slot (j*NA + a) % kQSlots, so while item j-1 runs, the first kQSlots-NA
+// atoms of item j can already be written into slots item j-1 does not use.
+__host__ __device__ inline bool q_fits_tmem(int NA) { return NA <= kQSlots; }
+__host__ __device__ inline int q_smem_bytes(int) { return kQStage * kHeads * 128; }
 
 struct Params {
   int B, S, H, D;      // D: qk head dim (multiple of 8)
@@ -96,7 +106,8 @@ struct __align__(8) Misc {
   uint64_t idx_full[kIdxSlots], idx_empty[kIdxSlots];
   uint32_t kvmask[8];             // valid-slot mask of the tile in each kv stage
   int idx_ring[kIdxSlots][32];    // selected kv rows of upcoming tiles (-1 = masked)
-  uint64_t q_full, q_empty;
+  uint64_t q_full[2], q_empty;  // q_full[j & 1]: item j's Q is in TMEM; q_empty: an item's Q.K^T completed
+  uint64_t qs_full[kQStage], qs_empty[kQStage];  // Q staging ring
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
   uint64_t pv_done[2], o_free;  // pv_done[b]: MMA2 that read P buffer b completed
@@ -109,14 +120,14 @@ __host__ __device__ inline int stage_bytes(int NA) { return NA * NK * 128; }
 
 template <int NK>
 __host__ __device__ inline int num_stages(int NA) {
-  const int fixed = 1024 + NA * kHeads * 128 + 2 * NK * 128 + (int)sizeof(Misc) + 64;
+  const int fixed = 1024 + q_smem_bytes(NA) + 2 * NK * 128 + (int)sizeof(Misc) + 64;
   int n = (kSmemMax - fixed) / stage_bytes<NK>(NA);
   return n > 8 ? 8 : n;
 }
 
 template <int NK>
 __host__ __device__ inline size_t smem_bytes(int NA) {
-  return 1024 + (size_t)NA * kHeads * 128 + (size_t)num_stages<NK>(NA) * stage_bytes<NK>(NA) + 2 * NK * 128 +
+  return 1024 + (size_t)q_smem_bytes(NA) + (size_t)num_stages<NK>(NA) * stage_bytes<NK>(NA) + 2 * NK * 128 +
          sizeof(Misc);
 }
 
@@ -341,8 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int NA = p.NA;
   const int NST = num_stages<NK>(NA);
   const int SB = stage_bytes<NK>(NA);
-  uint8_t* sQ = smem;                                   // [NA][64 rows][128 B], 128B swizzle
-  uint8_t* sKV = sQ + NA * kHeads * 128;                // [NST][NA][NK rows][128 B], 128B swizzle
+  uint8_t* sQ = smem;  // [kQStage][64 rows][128 B], 128B swizzle: Q staging ring
+  uint8_t* sKV = sQ + q_smem_bytes(NA);                 // [NST][NA][NK rows][128 B], 128B swizzle
   uint8_t* sP = sKV + (size_t)NST * SB;                 // [2][NK/8][8 row groups][8 rows][16 B]
   Misc* ms = reinterpret_cast<Misc*>(sP + 2 * NK * 128);
 
@@ -363,8 +374,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ms->idx_full[i], 32);                // every lane of the index warp
       mbar_init(&ms->idx_empty[i], kGatherWarps + 1);  // gather warps + TMA warp
     }
-    mbar_init(&ms->q_full, 1);
+    mbar_init(&ms->q_full[0], 4);  // one arrival per loader warp
+    mbar_init(&ms->q_full[1], 4);
     mbar_init(&ms->q_empty, 1);
+    for (int i = 0; i < kQStage; ++i) {
+      mbar_init(&ms->qs_full[i], 1);
+      mbar_init(&ms->qs_empty[i], 4);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ms->s_full[i], 1);
       mbar_init(&ms->s_free[i], 4);
@@ -391,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer: Q tile (TMA)
-    uint32_t qph = 0;
+    uint32_t qslot = 0, qsph = 0;
     for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
       const int hg = it % p.hgroups;
       const int bs = it / p.hgroups;
@@ -400,14 +416,90 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nrow = (nx / p.hgroups) * p.H + (nx % p.hgroups) * kHeads;
         tma_prefetch_l2_2d(&map_q, (int)lane * 64, nrow);
       }
-      if (!mbar_wait(&ms->q_empty, qph ^ 1, abort_flag, p.status, kErrWaitQ)) break;
-      qph ^= 1;
-      if (lane == 0) {
-        mbar_expect_tx(&ms->q_full, (uint32_t)NA * kHeads * 128);
-        const int qrow = bs * p.H + hg * kHeads;
-        for (int a = 0; a < NA; ++a) tma_load_2d(sQ + a * kHeads * 128, &map_q, &ms->q_full, a * 64, qrow);
+      const int qrow = bs * p.H + hg * kHeads;
+      // Q atoms through the staging ring; the loader warps move them to TMEM
+      bool ok = true;
+      for (int a = 0; a < NA; ++a) {
+        if (!mbar_wait(&ms->qs_empty[qslot], qsph ^ 1, abort_flag, p.status, kErrWaitQ)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_expect_tx(&ms->qs_full[qslot], (uint32_t)kHeads * 128);
+          tma_load_2d(sQ + qslot * kHeads * 128, &map_q, &ms->qs_full[qslot], a * 64, qrow);
+        }
+        __syncwarp();
+        if (++qslot == (uint32_t)kQStage) {
+          qslot = 0;
+          qsph ^= 1;
+        }
       }
-      __syncwarp();
+      if (!ok) break;
+    }
+  } else if (warp >= 9 + kGatherWarps) {
+    // ------------------------------------------------------------ Q loaders
+    // Warp w owns TMEM lane quarter w % 4: rows 16*(w%4) .. +15 of the 64-head
+    // group at lanes 16-31, beside S (the A operand of an M=64 MMA sits on the
+    // same lanes as its D).  Each staged atom (64 Q columns) goes in with one
+    // 16x32bx2 store per warp: thread i writes row i's columns [0,32) of the
+    // atom, thread 16+i columns [32,64) (two bf16 per 32-bit TMEM column).  An
+    // atom slot is rewritten only after the Q.K^T of the item that last used it
+    // completed (q_empty completions are counted in item order).
+    {
+      const int qd = warp & 3;
+      const int hrow = 16 * qd + (int)(lane & 15);
+      const uint32_t half = lane >> 4;
+      const uint32_t tq = tmem + ((uint32_t)(32 * qd + 16) << 16) + kQCol;
+      uint32_t qslot = 0, qsph = 0, done_items = 0;
+      bool ok = true;
+      auto wait_items_done = [&](int n) -> bool {  // Q.K^T of CTA-local items 0..n-1 complete
+        while ((int)done_items < n) {
+          if (!mbar_wait(&ms->q_empty, done_items & 1, abort_flag, p.status, kErrWaitQ)) return false;
+          ++done_items;
+        }
+        return true;
+      };
+      int jj = 0;
+      for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++jj) {
+        for (int a = 0; a < NA; ++a) {
+          const int g = jj * NA + a;
+          const int prev = g - kQSlots;  // atom that last used this slot
+          if (prev >= 0 && !wait_items_done(prev / NA + 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!mbar_wait(&ms->qs_full[qslot], qsph, abort_flag, p.status, kErrWaitQ)) {
+            ok = false;
+            break;
+          }
+          const uint8_t* rowp = sQ + qslot * kHeads * 128 + hrow * 128;
+          uint32_t v[16];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t c = 4 * half + (uint32_t)k;
+            const uint4 x = *reinterpret_cast<const uint4*>(rowp + ((c ^ (uint32_t)(hrow & 7)) << 4));
+            v[4 * k + 0] = x.x;
+            v[4 * k + 1] = x.y;
+            v[4 * k + 2] = x.z;
+            v[4 * k + 3] = x.w;
+          }
+          tmem_st16x32bx2_x16<16>(tq + (uint32_t)(g % kQSlots) * 32, v);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ms->qs_empty[qslot]);
+          if (++qslot == (uint32_t)kQStage) {
+            qslot = 0;
+            qsph ^= 1;
+          }
+        }
+        // q_full[jj & 1] was last consumed for item jj-2, whose Q.K^T began
+        // before item jj-2's completed
+        if (!ok || (jj >= 2 && !wait_items_done(jj - 1))) break;
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ms->q_full[jj & 1]);
+      }
     }
   } else if (warp == 6 + kGatherWarps) {
     // ------------------------------------------------------------ TMA row gathers (gather4) of atoms [0, na_tma)
@@ -560,16 +652,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // thread's MMAs) an S completion never waits for a P.V.
     if (lane == 0) {
       const uint32_t idesc1 = umma_idesc_f16(kHeads, NK, 1);
-      uint32_t st = 0, kph = 0, qph = 0;
+      uint32_t st = 0, kph = 0;
       uint32_t sfr[2] = {0, 0};
       bool ok = true;
-      const uint32_t qbase = smem_u32(sQ);
-      for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      int jj = 0;
+      for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++jj) {
 #ifdef SI_ATTN_TRACE
         const int ii = (it - (int)blockIdx.x) / (int)gridDim.x;
 #endif
-        if (!mbar_wait(&ms->q_full, qph, abort_flag, p.status, kErrWaitQ)) break;
-        qph ^= 1;
+        if (!mbar_wait(&ms->q_full[jj & 1], (uint32_t)(jj >> 1) & 1, abort_flag, p.status, kErrWaitQ)) break;
         tc_fence_after();
         for (int t = 0; t < ntiles; ++t) {
           SI_TRACE(1, ii, t, 0);
@@ -585,11 +676,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t kvbase = smem_u32(sKV + (size_t)st * SB);
           const uint32_t d_s = tmem + (16u << 16) + (t & 1) * NK;
+          const uint32_t a_q = tmem + (16u << 16) + kQCol;
           for (int a = 0; a < NA; ++a) {
+            const uint32_t a_col = a_q + (uint32_t)((jj * NA + a) % kQSlots) * 32;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              umma_f16(d_s, umma_desc_sw128(qbase + a * kHeads * 128 + kk * 32),
-                       umma_desc_sw128(kvbase + a * NK * 128 + kk * 32), idesc1, (a | kk) != 0);
+              umma_f16_tmem_a(d_s, a_col + kk * 8, umma_desc_sw128(kvbase + a * NK * 128 + kk * 32), idesc1,
+                              (a | kk) != 0);
             }
           }
           umma_commit(&ms->s_full[t & 1]);
@@ -711,7 +804,8 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
   if (!q || !kv || !attn_sink || !o || !ws) return fail("sparse_attn_fwd: null pointer");
   if (K > 0 && !topk_idxs) return fail("sparse_attn_fwd: null topk_idxs");
   if (B < 1 || S < 0 || H < 1 || Nkv < 0 || K < 0) return fail("sparse_attn_fwd: bad sizes");
-  if (D < 8 || D % 8 || D > 1024) return fail("sparse_attn_fwd: D must be a multiple of 8 in [8,1024] (got %d)", D);
+  if (D < 8 || D % 8 || D > attn::kQSlots * 64)
+    return fail("sparse_attn_fwd: D must be a multiple of 8 in [8,%d] (got %d)", attn::kQSlots * 64, D);
   if (Dv < 64 || Dv % 64 || Dv > ((D + 63) / 64) * 64 || Dv > D)
     return fail("sparse_attn_fwd: Dv must be a multiple of 64 with Dv <= D (got Dv=%d, D=%d)", Dv, D);
   if ((((uintptr_t)q) | ((uintptr_t)kv) | ((uintptr_t)o)) & 15) return fail("sparse_attn_fwd: 16-byte alignment");
@@ -719,7 +813,8 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
   if ((long long)B * S * H + 64 >= (1ll << 31) || (long long)B * Nkv + 1 >= (1ll << 31))
     return fail("sparse_attn_fwd: sizes exceed the 2^31 TMA coordinate range");
   const int NA = (D + 63) / 64;
-  if (attn::num_stages<32>(NA) < 2) return fail("sparse_attn_fwd: D=%d too large for the shared-memory plan", D);
+  if (!attn::q_fits_tmem(NA) || attn::num_stages<32>(NA) < 2)
+    return fail("sparse_attn_fwd: D=%d too large (Q must fit in tensor memory: D <= %d)", D, attn::kQSlots * 64);
   int* status = reinterpret_cast<int*>(ws);
   if (cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream)) return fail_cuda("sparse_attn_fwd: status", e);
   if (S == 0) return 0;
