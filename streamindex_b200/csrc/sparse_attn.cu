@@ -78,6 +78,7 @@ struct Params {
   int* status;
   int hgroups;         // ceil(H/64)
   int na_tma;          // leading atoms of each kv row gathered by TMA (warp 14); the rest by cp.async
+  int o_v8;            // o rows are 32-byte aligned: 256-bit output stores
   unsigned long long* trace;  // debug builds (SI_ATTN_TRACE) only: per-role timestamps of CTA 0
 };
 
@@ -318,18 +319,21 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       float v[32];
       tmem_ld16x32bx2_x32_sync<DVH>(tq + c * 32, v);
       if (head < p.H) {
+        uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 u;
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j + 0] * inv, v[j + 1] * inv);
-          __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2] * inv, v[j + 3] * inv);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4] * inv, v[j + 5] * inv);
-          __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6] * inv, v[j + 7] * inv);
-          u.x = *reinterpret_cast<uint32_t*>(&h0);
-          u.y = *reinterpret_cast<uint32_t*>(&h1);
-          u.z = *reinterpret_cast<uint32_t*>(&h2);
-          u.w = *reinterpret_cast<uint32_t*>(&h3);
-          *reinterpret_cast<uint4*>(orow + c * 32 + j) = u;
+        for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j] * inv, v[2 * j + 1] * inv);
+        __nv_bfloat16* dst = orow + c * 32;
+        if (p.o_v8) {  // two 32-byte stores: half the store transactions of 16-byte ones
+#pragma unroll
+          for (int j = 0; j < 16; j += 8)
+            asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst + 2 * j), "r"(w[j]),
+                         "r"(w[j + 1]), "r"(w[j + 2]), "r"(w[j + 3]), "r"(w[j + 4]), "r"(w[j + 5]), "r"(w[j + 6]),
+                         "r"(w[j + 7])
+                         : "memory");
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(w[j], w[j + 1], w[j + 2], w[j + 3]);
         }
       }
     }
@@ -836,6 +840,7 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
   p.Nkv1 = Nkv1;
   p.sink = attn_sink;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.o_v8 = (((uintptr_t)o) & 31) == 0 && (Dv * 2) % 32 == 0;  // row stride Dv, column offsets multiples of 64
   p.status = status;
   p.hgroups = (H + attn::kHeads - 1) / attn::kHeads;
 #ifdef SI_ATTN_TRACE
