@@ -38,3 +38,24 @@ def test_errors_are_reported_without_gpu():
     assert "null" in msg or "H_I" in msg
     rc = lib.si_indexer_topk(None, None, None, 0, 0, 1, 8, 8, 64, 128, 0, 4, None, None, None, None, 0, None)
     assert rc == -1 and "top_k" in lib.si_last_error().decode()
+
+
+def test_attention_argument_checks_without_gpu():
+    """Shape limits of si_sparse_attn_fwd are checked before any device work:
+    D must be a multiple of 8 up to 896 (Q lives in 14 TMEM atom slots) and Dv a
+    multiple of 64 no larger than D."""
+    import ctypes
+    from streamindex_b200 import _lib
+
+    lib = _lib.load()
+    dummy = ctypes.c_void_p(256)  # never dereferenced: the checks fail first
+
+    def call(D, Dv, H=64, K=8):
+        return lib.si_sparse_attn_fwd(dummy, dummy, ctypes.cast(dummy, ctypes.POINTER(ctypes.c_float)),
+                                      ctypes.cast(dummy, ctypes.POINTER(ctypes.c_int32)), 1, 4, H, D, 16, K, Dv,
+                                      0.1, dummy, None, dummy, 256, None)
+
+    assert call(960, 512) == -1 and "D must be" in lib.si_last_error().decode()
+    assert call(900, 512) == -1 and "D must be" in lib.si_last_error().decode()
+    assert call(576, 640) == -1 and "Dv" in lib.si_last_error().decode()
+    assert call(576, 96) == -1 and "Dv" in lib.si_last_error().decode()
