@@ -8,14 +8,15 @@
 //   denominator only).
 //
 // Mapping.  One persistent CTA per SM walks work items (b, s, 64-head group).
-// Q [64 heads x D] stays in shared memory for the item; the item's selected
-// KV rows (1152 bytes per index at D=576) are gathered NK at a time into
-// 128-byte-swizzled tiles that serve both GEMMs:
-//   MMA1  S[64 x NK]  = Q . KV^T           (M=64, K=D, A and B K-major)
+// The item's selected KV rows (1152 bytes per index at D=576) are gathered NK at
+// a time into 128-byte-swizzled shared-memory stages that serve both GEMMs:
+//   MMA1  S[64 x NK]  = Q . KV^T           (M=64, K=D; Q from TMEM, KV K-major)
 //   MMA2  O[64 x Dv] += P . V              (M=64, K=NK, P K-major, V MN-major)
-// With M=64 an accumulator occupies TMEM lanes 0-15 of each 32-lane quarter;
-// O lives there (lanes 0-15, columns [0,Dv)) and the two S buffers live in
-// lanes 16-31 (columns [0,2*NK)), so the whole TMEM is used without overlap.
+// With M=64 an accumulator occupies 16 lanes of each 32-lane TMEM quarter.  O
+// lives in lanes 0-15 (columns [0,Dv)); lanes 16-31 hold the two S buffers
+// (columns [0,2*NK)) and Q, the A operand of MMA1, which must sit on the same
+// lanes as S: its 64-column atoms fill a ring of 32-column slots after the S
+// buffers, so the next item's first atoms go in while the current item runs.
 //
 // Softmax warps (4, one per lane quarter = 16 heads): threads i and 16+i of a
 // warp share head row i, each taking 16 of the tile's 32 scores (16x32bx2 TMEM
@@ -26,14 +27,15 @@
 // shift) <= 256 stays well inside the bf16 range.  P goes to shared memory (bf16) as
 // the A operand of MMA2.
 //
-// Warp roles (544 threads): warp 0 TMA for the Q tile (and an L2 prefetch of
-// the next item's Q), warp 1 TMEM alloc + Q.K^T issue, warp 16 P.V issue, warps 2-5 softmax / O
-// correction / output, warps 6-13 kv row gathers with 16-byte cp.async
-// (completion signalled on the stage barrier with cp.async.mbarrier.arrive.noinc),
-// warp 14 TMA gather4 for the first atoms of each row (single kv tensor only) and
-// the per-stage valid-slot mask, warp 15 the index ring: it reads the selected
-// indices several tiles ahead into shared memory, so no gather thread waits on a
-// global load of an index.
+// Warp roles (672 threads): warp 0 TMA for Q atoms into a staging ring (and an
+// L2 prefetch of the next item's Q), warp 1 TMEM alloc + Q.K^T issue, warp 16
+// P.V issue, warps 2-5 softmax / O correction / output, warps 6-13 kv row
+// gathers with 16-byte cp.async (completion signalled on the stage barrier with
+// cp.async.mbarrier.arrive.noinc), warp 14 TMA gather4 for the first atoms of
+// each row (single kv tensor only) and the per-stage valid-slot mask, warp 15
+// the index ring (it reads the selected indices several tiles ahead into shared
+// memory, so no gather thread waits on a global load of an index), warps 17-20
+// move the staged Q atoms into TMEM.
 #include <cuda_bf16.h>
 
 #include "capi_common.h"
