@@ -93,3 +93,15 @@ def test_config4_full_size_sampled_queries():
         ro, _ = oracle.sparse_attn(q[:, s_:s_ + 1].cpu(), kv.cpu(), sink.cpu(), idx[:, s_:s_ + 1].cpu(), D ** -0.5,
                                    d_v=512)
         assert (o[:, s_:s_ + 1].float().cpu() - ro).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("B,S,H,D,K", [(2, 600, 64, 896, 48), (2, 700, 64, 200, 40), (1, 400, 128, 576, 64)])
+def test_q_atom_ring_many_items(B, S, H, D, K):
+    """Q sits in tensor memory in a ring of 14 atom slots (64 qk columns each);
+    each CTA walks many work items here, so the ring wraps many times: D=896
+    fills all 14 slots (no atom of the next item can be preloaded), D=200 is
+    not a multiple of 64 (zero-filled tail atom, 10 atoms preloadable), and
+    H=128 gives two 64-head items per query."""
+    q, kv, sink, idx = oracle.attn_inputs(B, S, H, D, 300, K, ratio=1, seed=D + H)
+    idx[:, :, 5::7] = -1
+    _check(q, kv, sink, idx)
