@@ -1,6 +1,6 @@
 """StreamIndex-B200 benchmark: V4-Flash lightning indexer + top-k.
 
-Workload (the headline point): B=1, S=1,048,576,
+Workload (benchmark configs[1], the headline point): B=1, S=1,048,576,
 H_I=64, D_I=128, m=4 (T=S/4), top_k=512, causal t < (s+1)//4; synthetic
 inputs q, k ~ N(0,1)*D^-0.5 (bf16), w ~ N(0,1) (fp32), seeded, generated on
 the device.  One step = one indexer+top-k pass over the whole query range.
@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--attn-heads", type=int, default=64, help="attention workload: query heads (64; 128 = V4-Pro)")
     ap.add_argument("--attn-k", type=int, default=512, help="attention workload: selected kv rows per query")
     ap.add_argument("--workload", default="indexer", choices=["indexer", "attn", "csa"],
-                    help="indexer: the headline metric (default); attn: BASELINE configs[3] sparse attention")
+                    help="indexer: the headline metric (default); attn: benchmark configs[3] sparse attention")
     return ap.parse_args()
 
 
@@ -210,7 +210,7 @@ def run_reference(a, world, rank):
     print(json.dumps(line), flush=True)
 
 
-# published single-H200 Triton times for this workload, ms
+# published single-H200 Triton times for this workload (reference benchmarks/results/2026-04-27/scaling_v4_flash_indexer_final.log), ms
 PUBLISHED_H200_MS = {32768: 30.8, 65536: 122.2, 131072: 484.7, 262144: 1935.3, 524288: 7730.1, 1048576: 30899.6}
 
 
@@ -422,7 +422,7 @@ def gen_attn_idx(S, K, n_kv, ratio, device, seed=0, chunk=4096):
 
 
 def run_attn(a):
-    """sparse attention forward, B=1, S=65536, H=64, D=576/512, N_kv=16384, K=512."""
+    """benchmark configs[3]: sparse attention forward, B=1, S=65536, H=64, D=576/512, N_kv=16384, K=512."""
     from streamindex_b200 import _lib
 
     S, H, D, DV, NKV, K = a.S, a.attn_heads, 576, 512, 16384, a.attn_k
@@ -476,7 +476,7 @@ def run_attn(a):
                        d_v=DV)
     cpu_s = time.perf_counter() - t
     line = {
-        "metric": "sparse attention forward (BASELINE configs[3]) Mqueries/s", "value": S / (ms * 1e-3) / 1e6,
+        "metric": "sparse attention forward (benchmark configs[3]) Mqueries/s", "value": S / (ms * 1e-3) / 1e6,
         "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; causal uniform indices without replacement)",
@@ -494,26 +494,50 @@ def run_attn(a):
     print(json.dumps(line), flush=True)
 
 
-def run_csa(a, world=1, rank=0, local=0):
-    """CSA layer forward, B=2, S=131072, H=64, D=576/512, H_I=64, D_I=128, m=4, k=512, n_win=128.
+def _csa_slots(S, lo, hi, nwin, k, m):
+    """Valid attention slots of queries [lo, hi): window min(n_win, s+1) + compressed min(k, (s+1)//m)."""
+    import numpy as np
 
-    One step = mean-pool compressor (kv and indexer keys) -> fused indexer + top-k
-    -> index build -> sparse attention.  With N GPUs the query range is
-    S-sharded (work-balanced slices): rank 0 compresses and broadcasts the
-    compressed kv / keys, every rank runs its slice (``csa_forward_slice``) and
-    the outputs are gathered to rank 0."""
+    s = np.arange(lo, hi, dtype=np.int64)
+    return int(np.minimum(nwin, s + 1).sum() + np.minimum(k, np.minimum(S // m, (s + 1) // m)).sum())
+
+
+def _load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def run_csa(a, world=1, rank=0, local=0):
+    """benchmark configs[4]: CSA layer forward, B=2, S=131072, H=64, D=576/512, H_I=64, D_I=128, m=4, k=512, n_win=128.
+
+    One step = mean-pool compressors (kv and indexer keys) -> fused indexer + top-k
+    -> sparse attention with the window + compressed index list built in the
+    kernel.  With N GPUs the query range is S-sharded (work-balanced slices):
+    every rank holds the full x_kv / x_k, computes both compressors itself (no
+    broadcast), runs its slice (``csa_forward_slice``) and keeps its attention
+    output (the next layer consumes it sharded); the compressed top-k indices
+    are gathered to rank 0 (NCCL point-to-point), the one exchange the
+    north-star contract names.  Timed twice: with the index gather (the
+    headline) and without it."""
+    from streamindex_b200.attention import _csa_attn_call
     from streamindex_b200.csa import csa_forward_slice, flash_csa_forward, mean_pool_compress
-    from streamindex_b200.dist import balanced_bounds, broadcast_keys, gather_to_rank0
+    from streamindex_b200.dist import balanced_bounds, gather_to_rank0, legal_pairs
+    from streamindex_b200.indexer import indexer_topk_slice
 
     B, S, H, D, DV, HI, DI, m, k, nwin = 2, a.S, 64, 576, 512, 64, 128, 4, 512, 128
+    T = S // m
     dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     x_kv = torch.randn((B, S, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
     x_k = torch.randn((B, S, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
     # attention work per query relative to one indexer key: (n_win + k) * H * (D + DV) vs H_I * D_I flops
     extra = (nwin + k) * H * (D + DV) / (HI * DI)
-    bounds = balanced_bounds(S, world, S // m, m, align=128, extra_per_query=extra)
+    bounds = balanced_bounds(S, world, T, m, align=128, extra_per_query=extra)
     lo, hi = bounds[rank], bounds[rank + 1]
     gq = torch.Generator(device=dev)
     gq.manual_seed(100 + rank)
@@ -521,49 +545,212 @@ def run_csa(a, world=1, rank=0, local=0):
     q_idx = torch.randn((B, hi - lo, HI, DI), generator=gq, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
     w = torch.randn((B, hi - lo, HI), generator=gq, device=dev, dtype=torch.float32)
     sink = torch.zeros(H, dtype=torch.float32, device=dev)
-    kvc = torch.empty((B, S // m, D), dtype=torch.bfloat16, device=dev)
-    kc = torch.empty((B, S // m, DI), dtype=torch.bfloat16, device=dev)
-    full = torch.empty((B, S, H, DV), dtype=torch.bfloat16, device=dev) if (world > 1 and rank == 0) else None
+    comp_full = torch.empty((B, S, k), dtype=torch.int64, device=dev) if (world > 1 and rank == 0) else None
 
-    def step():
+    def step(gather):
+        kvc = mean_pool_compress(x_kv, m)
+        kc = mean_pool_compress(x_k, m)
         if world == 1:
-            kvc.copy_(mean_pool_compress(x_kv, m))
-            kc.copy_(mean_pool_compress(x_k, m))
             return flash_csa_forward(q, x_kv, kvc, q_idx, kc, w, sink, n_win=nwin, top_k=k, m=m, d_v=DV)
-        if rank == 0:
-            kvc.copy_(mean_pool_compress(x_kv, m))
-            kc.copy_(mean_pool_compress(x_k, m))
-        broadcast_keys(kvc)
-        broadcast_keys(kc)
-        o = csa_forward_slice(q, x_kv, kvc, q_idx, kc, w, sink, s_offset=lo, n_win=nwin, top_k=k, m=m, d_v=DV)
-        gather_to_rank0(o, bounds, full, dim=1)
+        o, comp = csa_forward_slice(q, x_kv, kvc, q_idx, kc, w, sink, s_offset=lo, n_win=nwin, top_k=k, m=m, d_v=DV,
+                                    return_indices=True)
+        if gather:
+            gather_to_rank0(comp, bounds, comp_full, dim=1)
         return o
 
+    def timed(gather, clocks=None):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _barrier_sync(world)
+        if clocks:
+            clocks.start()
+        t0.record()
+        for _ in range(a.steps):
+            step(gather)
+        t1.record()
+        _barrier_sync(world)
+        clk = clocks.stop() if clocks else None
+        return _max_over_ranks(t0.elapsed_time(t1) / a.steps, world, dev), clk
+
+    gather = world > 1 and not a.no_gather
     for _ in range(a.warmup):
-        step()
-    clocks = ClockSampler(local)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    _barrier_sync(world)
-    clocks.start()
-    t0.record()
-    for _ in range(a.steps):
-        step()
-    t1.record()
-    _barrier_sync(world)
-    clk = clocks.stop()
-    ms = _max_over_ranks(t0.elapsed_time(t1) / a.steps, world, dev)
+        step(gather)
+    ms, clk = timed(gather, ClockSampler(local))
+    ms_nogather = timed(False)[0] if gather else ms
+
+    # per-kernel split on this rank (same calls, events between them)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    kern = {"mean_pool_x2_ms": 0.0, "indexer_topk_ms": 0.0, "csa_attention_ms": 0.0}
+    reps = max(1, min(a.steps, 5))
+    for _ in range(reps):
+        ev[0].record()
+        kvc = mean_pool_compress(x_kv, m)
+        kc = mean_pool_compress(x_k, m)
+        ev[1].record()
+        comp, _ = indexer_topk_slice(q_idx, kc, w, k, m, lo)
+        ev[2].record()
+        _csa_attn_call(q, x_kv, kvc, sink, comp, nwin, lo, D ** -0.5, DV)
+        ev[3].record()
+        torch.cuda.synchronize()
+        kern["mean_pool_x2_ms"] += ev[0].elapsed_time(ev[1]) / reps
+        kern["indexer_topk_ms"] += ev[1].elapsed_time(ev[2]) / reps
+        kern["csa_attention_ms"] += ev[2].elapsed_time(ev[3]) / reps
+
+    # algorithmic work of this rank's slice (rank 0 reports its own; all ranks are balanced)
+    idx_flops = B * 2.0 * HI * DI * legal_pairs(S, T, m, lo, hi)
+    att_flops = B * 2.0 * H * (D + DV) * _csa_slots(S, lo, hi, nwin, k, m)
+    peaks = _load_peaks()
+    tf_peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    src = ("of measured (bf16_tflops_sustained, MEASURED_PEAKS.json: the step repeats for seconds under the power cap)"
+           if peaks.get("bf16_tflops_sustained") else "of fallback (1.4 PFLOP/s sustained)")
+    step_local_ms = kern["mean_pool_x2_ms"] + kern["indexer_topk_ms"] + kern["csa_attention_ms"]
+    achieved = (idx_flops + att_flops) / (step_local_ms * 1e-3) / 1e12
+
+    peak_gb = None
+    if world == 1:
+        del comp, kvc, kc
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats(dev)
+        base = torch.cuda.memory_allocated(dev)
+        o = step(False)
+        torch.cuda.synchronize()
+        peak_gb = (torch.cuda.max_memory_allocated(dev) - base) / 1e9
+        del o
+
+    e2e = None if (a.no_e2e or world > 1) else run_csa_e2e(a, q, q_idx, w, x_kv, x_k, sink, dev)
+    cpu = None if (a.no_cpu or world > 1 or rank != 0) else run_csa_cpu(q, q_idx, w, x_kv, x_k, sink, m, nwin, k)
     if rank == 0:
         line = {
-            "metric": "CSA layer forward (BASELINE configs[4]) Mqueries/s", "value": B * S / (ms * 1e-3) / 1e6,
+            "metric": "CSA layer forward (benchmark configs[4]) Mqueries/s", "value": B * S / (ms * 1e-3) / 1e6,
             "unit": "Mqueries/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "ms_per_step_no_gather": ms_nogather, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1)*D^-0.5 bf16 activations, N(0,1) fp32 head weights, on device)",
             "config": {"workload": f"flash_csa_forward B=2 S={S} H=64 D=576/512 H_I=64 D_I=128 m=4 top_k=512 n_win=128",
-                       "path": "mean-pool x2 -> fused indexer+top-k -> index build -> split-kv sparse attention",
-                       "parallelism": f"S-shard x{world} (compressed kv/keys broadcast, output gathered)"
-                       if world > 1 else "single GPU"},
+                       "path": "mean-pool x2 -> fused indexer+top-k -> sparse attention with the index list built "
+                               "in the kernel (window + compressed picks)",
+                       "parallelism": (f"S-shard x{world}: compressors on every rank, output kept sharded, "
+                                       f"compressed top-k indices gathered to rank 0"
+                                       + (" (gather off)" if a.no_gather else "")) if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (q is 19 GB)"},
+            "gpu_launches": 5 * a.steps,
+            "kernels": kern,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": achieved / tf_peak, "peak_source": src, "traffic": None,
+                         "algorithmic": "indexer 2*H_I*D_I per legal (s,t) pair + attention 2*H*(D+D_v) per valid "
+                                        "slot, over the step's summed kernel times on rank 0",
+                         "indexer_tflops": idx_flops / (kern["indexer_topk_ms"] * 1e-3) / 1e12,
+                         "attention_tflops": att_flops / (kern["csa_attention_ms"] * 1e-3) / 1e12},
+            "peak_hbm_gb": peak_gb,
             "clocks": clk,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+
+
+def run_csa_e2e(a, q, q_idx, w, x_kv, x_k, sink, dev, chunk=8192):
+    """CSA step through the public API with HOST (pinned) inputs and output.
+
+    Each step copies x_kv / x_k to the device, compresses them, then walks the
+    query range in chunks of one batch row: H2D of chunk c+1 (copy stream) and
+    D2H of chunk c-1's output (second copy stream) overlap the layer forward of
+    chunk c (``csa_forward_slice`` with the chunk's global offset)."""
+    from streamindex_b200.csa import csa_forward_slice, mean_pool_compress
+
+    B, S, H, D = q.shape
+    DV, m, k, nwin = 512, 4, 512, 128
+    pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t)  # noqa: E731
+    hq, hqi, hw, hkv, hk = pin(q), pin(q_idx), pin(w), pin(x_kv), pin(x_k)
+    ho = torch.empty((B, S, H, DV), dtype=torch.bfloat16, pin_memory=True)
+    del q, q_idx, w
+    torch.cuda.empty_cache()
+    cs = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    chunks = [(b, s0, min(S, s0 + chunk)) for b in range(B) for s0 in range(0, S, chunk)]
+    kvd = torch.empty_like(x_kv)
+    kd = torch.empty_like(x_k)
+
+    def one():
+        kvd.copy_(hkv, non_blocking=True)
+        kd.copy_(hk, non_blocking=True)
+        kvc, kc = mean_pool_compress(kvd, m), mean_pool_compress(kd, m)
+        staged = {}
+
+        def stage(i):
+            b, s0, s1 = chunks[i]
+            with torch.cuda.stream(up):
+                t = (hq[b:b + 1, s0:s1].to(dev, non_blocking=True), hqi[b:b + 1, s0:s1].to(dev, non_blocking=True),
+                     hw[b:b + 1, s0:s1].to(dev, non_blocking=True))
+                e = torch.cuda.Event()
+                e.record(up)
+            staged[i] = (t, e)
+
+        stage(0)
+        for i, (b, s0, s1) in enumerate(chunks):
+            if i + 1 < len(chunks):
+                stage(i + 1)
+            (tq, tqi, tw), e = staged.pop(i)
+            cs.wait_event(e)
+            for t in (tq, tqi, tw):
+                t.record_stream(cs)
+            o = csa_forward_slice(tq, kvd[b:b + 1], kvc[b:b + 1], tqi, kc[b:b + 1], tw, sink, s_offset=s0,
+                                  n_win=nwin, top_k=k, m=m, d_v=DV)
+            down.wait_stream(cs)
+            with torch.cuda.stream(down):
+                ho[b:b + 1, s0:s1].copy_(o, non_blocking=True)
+            o.record_stream(down)
+        cs.wait_stream(down)
+
+    one()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(a.e2e_steps):
+        one()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / a.e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hqi, hw, hkv, hk))
+    d2h = ho.numel() * ho.element_size()
+    return {"value": B * S / (ms * 1e-3) / 1e6, "unit": "Mqueries/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": a.e2e_steps,
+            "path": f"pinned host inputs -> x_kv/x_k H2D + mean-pool, then {len(chunks)} query chunks: H2D of "
+                    "chunk c+1 and D2H of chunk c-1's output overlapped with csa_forward_slice on chunk c"}
+
+
+def run_csa_cpu(q, q_idx, w, x_kv, x_k, sink, m, nwin, k, n=6):
+    """The reference's CSA forward (oracle restatement of flash_sparse/csa.py:86-207) on n sampled queries of
+    batch 0: compressors over the whole sequence, materialised indexer scores over all compressed keys, mask,
+    top-k, window + compressed index list, sparse attention."""
+    import oracle
+    from oracle.csa import compressed_to_global
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    S = q.shape[1]
+    D = q.shape[-1]
+    pos = torch.linspace(0, S - 1, n).long()
+    qs, qis, ws_ = (t[0:1, pos.to(t.device)].cpu() for t in (q, q_idx, w))
+    xkv, xk = x_kv[0:1].cpu(), x_k[0:1].cpu()
+    t = time.perf_counter()
+    kvc = oracle.mean_pool_compress(xkv, m)
+    kc = oracle.mean_pool_compress(xk, m)
+    T = kc.shape[1]
+    sc = oracle.lightning_indexer(qis, kc, ws_)
+    lim = torch.clamp((pos + 1) // m, max=T)
+    sc = sc.masked_fill((torch.arange(T).view(1, -1) >= lim.view(-1, 1)).unsqueeze(0), float("-inf"))
+    ti, tv = oracle.topk_desc_stable(sc, min(k, T))
+    ti = torch.where(torch.isinf(tv), torch.full_like(ti, -1), ti)
+    win = (pos.view(-1, 1) - nwin + 1 + torch.arange(nwin).view(1, -1))
+    win = torch.where(win >= 0, win, torch.full_like(win, -1)).unsqueeze(0)
+    idx = torch.cat([win, compressed_to_global(ti, S)], dim=-1).int()
+    oracle.sparse_attn(qs, torch.cat([xkv, kvc], dim=1), sink.cpu(), idx, D ** -0.5, d_v=512)
+    dt = time.perf_counter() - t
+    return {"value": n / dt / 1e6, "unit": "Mqueries/s", "cores": threads, "kind": "port",
+            "sample": f"{n} queries of batch 0 evenly spaced over S={S}: oracle compressors + materialised indexer "
+                      f"over all {T} compressed keys + mask + top-{k} + window/compressed list + sparse attention, "
+                      f"{dt:.2f} s, torch threads={threads}"}
 
 
 def main():

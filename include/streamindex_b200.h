@@ -100,6 +100,10 @@ SI_API int si_indexer_topk_noalloc(const void* q, const void* k, const void* w, 
                                    int S, int T, int H, int D, int top_k, int causal_ratio,
                                    const uint8_t* causal_mask, int64_t* out_idx, float* out_scores,
                                    cudaStream_t stream);
+/* Status word of the allocation-free path (0 = ok, non-zero = a bounded wait
+ * inside the last si_indexer_topk_noalloc kernel on this device timed out and
+ * its results are incomplete).  Synchronises `stream`; allocates nothing. */
+SI_API int si_indexer_topk_noalloc_read_status(int* status_out, cudaStream_t stream);
 
 /* Materialised indexer scores, no mask.
  * Replaces indexer_score (flash_sparse/triton/indexer_score.py:123-179).
@@ -129,6 +133,26 @@ SI_API int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const 
                                   const float* attn_sink, const int32_t* topk_idxs, int B, int S, int H, int D, int K,
                                   int Dv, float softmax_scale, void* o, float* lse, void* ws, size_t ws_bytes,
                                   cudaStream_t stream);
+
+/* CSA sparse attention with the index list built inside the kernel.
+ * Replaces the index concatenation of flash_csa_forward
+ * (flash_sparse/csa.py:176-179, window of flash_sparse/reference.py:460-475)
+ * followed by its sparse_attn call (flash_sparse/csa.py:199-205), without
+ * materialising the [B,S,n_win+top_k] int32 list or cat[kv; kv_comp]:
+ *   q        [B,S,H,D]   bf16   the query slice [s_offset, s_offset+S) of a
+ *                               sequence of S_total tokens (S_total = S and
+ *                               s_offset = 0 for a whole sequence)
+ *   kv       [B,S_total,D]  bf16     window rows
+ *   kv_comp  [B,T,D]        bf16     compressed rows
+ *   comp_idx [B,S,top_k]    int64    compressed top-k picks (-1 = empty), as
+ *                                    returned by si_indexer_topk_ex(s_offset)
+ * Slot j < n_win reads kv[p - n_win + 1 + j] for global position p (masked
+ * if negative); slot n_win + j reads kv_comp[comp_idx[.., j]] (masked if -1).
+ * Everything else as si_sparse_attn_fwd. */
+SI_API int si_csa_sparse_attn_fwd(const void* q, const void* kv, int S_total, const void* kv_comp, int T,
+                                  const float* attn_sink, const int64_t* comp_idx, int top_k, int n_win,
+                                  long long s_offset, int B, int S, int H, int D, int Dv, float softmax_scale, void* o,
+                                  float* lse, void* ws, size_t ws_bytes, cudaStream_t stream);
 
 /* Top-k of a materialised score matrix [B,S,T] fp32 with the causal limit
  * t < (s+1)/causal_ratio (<= 0: none); same output contract as si_indexer_topk.

@@ -32,5 +32,7 @@ from .csa import (  # noqa: F401
     hca_forward,
     token_compressor,
 )
-from .metrics import set_recall, norm_corr, score_close  # noqa: F401
+from .metrics import (  # noqa: F401
+    set_recall, norm_corr, score_close, exact_pair_scores, measured_score_error, topk_tie_violations,
+)
 from .inputs import indexer_inputs, attn_inputs  # noqa: F401

@@ -33,11 +33,15 @@ SIGNATURES = {
     "si_indexer_topk_noalloc_max_ws_bytes": (c_size_t, []),
     "si_indexer_topk_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "si_indexer_topk_noalloc_read_status": (c_int, [ctypes.POINTER(c_int), c_void_p]),
     "si_sparse_attn_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                    c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "si_sparse_attn_fwd_kv2": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
                                        c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t,
                                        c_void_p]),
+    "si_csa_sparse_attn_fwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
+                                       ctypes.c_longlong, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
+                                       c_void_p, c_void_p, c_size_t, c_void_p]),
     "si_scores_topk_ws_bytes": (c_size_t, [c_int, c_int, c_int]),
     "si_scores_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
                                c_void_p]),

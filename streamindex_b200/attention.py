@@ -54,6 +54,36 @@ def _attn_call(q, kv, kv2, attn_sink, idx, softmax_scale, dv):
     return o, lse
 
 
+def _csa_attn_call(q, kv, kv_comp, attn_sink, comp_idx, n_win, s_offset, softmax_scale, dv):
+    """CSA attention with the window + compressed index list built in the kernel
+    (``si_csa_sparse_attn_fwd``).  ``q`` is the query slice starting at global
+    position ``s_offset`` of the ``kv.shape[1]``-token sequence; ``comp_idx``
+    ``[B,S,top_k]`` int64 holds the compressed picks (-1 = empty)."""
+    B, S, H, D = q.shape
+    dev = q.device
+    top_k = comp_idx.shape[-1]
+    dv_k = ((dv + 63) // 64) * 64
+    Dp = ((max(D, dv_k) + 7) // 8) * 8
+    qk, kvk, kck = q.contiguous(), kv.contiguous(), kv_comp.contiguous()
+    if Dp != D:
+        qk, kvk, kck = F.pad(qk, (0, Dp - D)), F.pad(kvk, (0, Dp - D)), F.pad(kck, (0, Dp - D))
+    comp = comp_idx.to(device=dev, dtype=torch.int64).contiguous()
+    sink = attn_sink.to(device=dev, dtype=torch.float32).contiguous()
+    o = torch.empty((B, S, H, dv_k), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, S, H), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(256, dtype=torch.uint8, device=dev)
+        _lib.check(lib.si_csa_sparse_attn_fwd(
+            qk.data_ptr(), kvk.data_ptr(), kvk.shape[1], kck.data_ptr(), kck.shape[1], sink.data_ptr(),
+            comp.data_ptr() if top_k > 0 else None, top_k, int(n_win), int(s_offset), B, S, H, Dp, dv_k,
+            float(softmax_scale), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, _lib.stream_handle(dev)))
+        _lib.maybe_check_status(ws, dev, "csa_sparse_attn_fwd")
+    if dv_k != dv:
+        o = o[..., :dv].contiguous()
+    return o, lse
+
+
 def sparse_attn_fwd(
     q: torch.Tensor,
     kv: torch.Tensor,

@@ -4,7 +4,8 @@ Mirrors ``flash_sparse/csa.py:30-207`` of the reference:
 
 1. indexer + top-k over the compressed keys with the causal mask
    ``(i+1)*m - 1 <= s``  (== ``i < (s+1)//m``), -1 for empty slots,
-2. index list ``[window(n_win) | compressed + S]`` int32,
+2. index list ``[window(n_win) | compressed + S]``, built inside the
+   attention kernel's index ring from the top-k output (never materialised),
 3. sparse attention over ``cat[kv; kv_compressed]`` with the attention sink.
 
 The reference picks between a materialised ``[B,S,T]`` score path and the
@@ -21,7 +22,7 @@ from typing import Optional
 import torch
 
 from . import _lib
-from .attention import _attn_call
+from .attention import _csa_attn_call
 from .indexer import chunked_indexer_topk, indexer_topk_slice
 
 
@@ -159,9 +160,8 @@ def flash_csa_forward(
     if softmax_scale is None:
         softmax_scale = d ** -0.5
     comp, _ = chunked_indexer_topk(q_idx, k_idx_compressed, indexer_weights, top_k, causal_ratio=m)
-    idx = csa_index_list(comp, n_win)
     dv = d if d_v is None else int(d_v)
-    o, _ = _attn_call(q, kv, kv_compressed, attn_sink, idx, softmax_scale, dv)
+    o, _ = _csa_attn_call(q, kv, kv_compressed, attn_sink, comp, n_win, 0, softmax_scale, dv)
     return o
 
 
@@ -180,7 +180,8 @@ def csa_forward_slice(
     m: int = 4,
     softmax_scale: Optional[float] = None,
     d_v: Optional[int] = None,
-) -> torch.Tensor:
+    return_indices: bool = False,
+):
     """CSA forward for the query slice ``[s_offset, s_offset + q.shape[1])`` of a sequence.
 
     ``q`` / ``q_idx`` / ``indexer_weights`` hold only the slice; ``kv`` (all
@@ -188,18 +189,16 @@ def csa_forward_slice(
     Causality, the window and the compressed offset use global positions, so
     concatenating the slices' outputs equals :func:`flash_csa_forward` on the
     whole sequence.  This is what each rank runs in the S-sharded CSA forward.
+    With ``return_indices`` it also returns the slice's compressed top-k
+    indices ``[B,S_loc,top_k]`` int64 (the per-rank result an index gather
+    collects).
     """
     B, S_loc, n_h, d = q.shape
-    S_total = kv.shape[1]
     if softmax_scale is None:
         softmax_scale = d ** -0.5
     comp, _ = indexer_topk_slice(q_idx, k_idx_compressed, indexer_weights, top_k, m, s_offset)
-    comp = comp.contiguous()
-    idx = torch.empty((B, S_loc, n_win + top_k), dtype=torch.int32, device=q.device)
-    lib = _lib.load()
-    with torch.cuda.device(q.device):
-        _lib.check(lib.si_csa_build_idx_ex(comp.data_ptr(), B, S_loc, int(s_offset), S_total, top_k, int(n_win),
-                                           idx.data_ptr(), _lib.stream_handle(q.device)))
     dv = d if d_v is None else int(d_v)
-    o, _ = _attn_call(q, kv, kv_compressed, attn_sink, idx, softmax_scale, dv)
+    o, _ = _csa_attn_call(q, kv, kv_compressed, attn_sink, comp, n_win, s_offset, softmax_scale, dv)
+    if return_indices:
+        return o, comp
     return o

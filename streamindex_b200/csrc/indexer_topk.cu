@@ -1068,6 +1068,14 @@ int si_indexer_topk_noalloc(const void* q, const void* k, const void* w, int w_i
                          causal_mask, mode, out_idx, out_scores, ws, si::kNoAllocScratchBytes, stream);
 }
 
+int si_indexer_topk_noalloc_read_status(int* status_out, cudaStream_t stream) {
+  if (!status_out) return si::fail("indexer_topk_noalloc_read_status: null pointer");
+  int rc = 0;
+  void* ws = si::noalloc_scratch_ptr(&rc);
+  if (!ws) return rc;
+  return si_read_status(ws, status_out, stream);
+}
+
 }  // extern "C"
 
 // ==================================================================== top-k over a score matrix

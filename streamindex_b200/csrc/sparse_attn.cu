@@ -71,7 +71,15 @@ struct Params {
   int Dv, dv_off;      // value columns [dv_off, dv_off+Dv) of kv (multiples of 64)
   int o_ld, o_off;     // output row stride (elements) and column offset
   float scale_log2;    // softmax_scale * log2(e)
-  const int* idx;      // [B,S,K]
+  const int* idx;      // [B,S,K] (explicit index list), or null with comp set
+  // CSA index list built in the index ring instead of read from idx (the
+  // concatenation of flash_sparse/csa.py:176-179 with the window of
+  // flash_sparse/reference.py:460-475): slot kk < nwin is the window position
+  // s_glob - nwin + 1 + kk (-1 if negative), slot nwin + j the compressed pick
+  // comp[b, s, j] offset by Nkv1 (-1 kept).  K = nwin + comp_k.
+  const long long* comp;  // [B,S,comp_k] int64 or null
+  int comp_k, nwin;
+  long long s_off;      // global position of local query 0
   const __nv_bfloat16* kv;   // [B,Nkv1,D]
   const __nv_bfloat16* kv2;  // [B,Nkv-Nkv1,D] or null
   const float* sink;   // [H]
@@ -310,11 +318,15 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
     issued_base[1] += (uint32_t)(ntiles >> 1);
 
     // ---- epilogue: sink in the denominator, normalise, write O and LSE
+    // The shift becomes max(m, sink) (sparse_attn_fwd.py:152-156), so a sink far
+    // above every score cannot overflow the denominator.
     if (m_used == -INFINITY) m_used = sink2;  // no valid key: O = 0, l = exp(sink - sink)
-    const float l_tot = l + exp2f(sink2 - m_used);
-    const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+    const float m_fin = fmaxf(m_used, sink2);
+    const float o_scale = exp2f(m_used - m_fin);
+    const float l_tot = l * o_scale + exp2f(sink2 - m_fin);
+    const float inv = l_tot > 0.f ? o_scale / l_tot : 0.f;
     if (half == 0 && head < p.H && p.lse)
-      p.lse[(size_t)bs * p.H + head] = l_tot > 0.f ? (m_used + log2f(l_tot)) * kLn2 : -1.0e30f;
+      p.lse[(size_t)bs * p.H + head] = l_tot > 0.f ? (m_fin + log2f(l_tot)) * kLn2 : -1.0e30f;
     __nv_bfloat16* orow = p.o + ((size_t)bs * p.H + head) * p.o_ld + p.o_off + half * DVH;
 #pragma unroll 1
     for (int c = 0; c < DVH / 32; ++c) {
@@ -569,12 +581,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int bs = it / p.hgroups;
       const int b = bs / p.S, s = bs % p.S;
       const int* src = p.idx + ((size_t)b * p.S + s) * p.K;
+      const long long* csrc = p.comp + ((size_t)b * p.S + s) * p.comp_k;
+      const long long s_glob = p.s_off + s;
       for (int t0 = 0; t0 < ntiles && ok; t0 += 8) {
         int v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int kk = (t0 + j) * NK + (int)lane;
-          v[j] = kk < p.K ? src[kk] : -1;
+          if (p.comp == nullptr) {
+            v[j] = kk < p.K ? src[kk] : -1;
+          } else if (kk < p.nwin) {
+            const long long pos = s_glob - p.nwin + 1 + kk;
+            v[j] = pos >= 0 ? (int)pos : -1;
+          } else if (kk < p.K) {
+            const long long c = csrc[kk - p.nwin];
+            v[j] = c >= 0 ? (int)(c + p.Nkv1) : -1;
+          } else {
+            v[j] = -1;
+          }
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -799,16 +823,19 @@ extern "C" SI_API void si_debug_set_attn_trace(unsigned long long* t) { g_attn_t
 
 extern "C" {
 
-int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
-                           const int32_t* topk_idxs, int B, int S, int H, int D, int K, int Dv, float softmax_scale,
-                           void* o, float* lse, void* ws, size_t ws_bytes, cudaStream_t stream) {
-  using namespace si;
+}  // extern "C"
+
+namespace si {
+static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
+                           const int32_t* topk_idxs, const int64_t* comp, int comp_k, int nwin, long long s_off,
+                           int B, int S, int H, int D, int K, int Dv, float softmax_scale, void* o, float* lse,
+                           void* ws, size_t ws_bytes, cudaStream_t stream) {
   if (Nkv2 < 0 || (Nkv2 > 0 && !kv2)) return fail("sparse_attn_fwd: bad second kv tensor");
   if (Nkv2 > 0 && (((uintptr_t)kv2) & 15)) return fail("sparse_attn_fwd: 16-byte alignment of kv2");
   const int Nkv1 = Nkv;
   Nkv = Nkv1 + Nkv2;
-  if (!q || !kv || !attn_sink || !o || !ws) return fail("sparse_attn_fwd: null pointer");
-  if (K > 0 && !topk_idxs) return fail("sparse_attn_fwd: null topk_idxs");
+  if (!q || (Nkv1 > 0 && !kv) || !attn_sink || !o || !ws) return fail("sparse_attn_fwd: null pointer");
+  if (K > 0 && !topk_idxs && !comp) return fail("sparse_attn_fwd: null topk_idxs");
   if (B < 1 || S < 0 || H < 1 || Nkv < 0 || K < 0) return fail("sparse_attn_fwd: bad sizes");
   if (D < 8 || D % 8 || D > attn::kQSlots * 64)
     return fail("sparse_attn_fwd: D must be a multiple of 8 in [8,%d] (got %d)", attn::kQSlots * 64, D);
@@ -824,10 +851,15 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
   int* status = reinterpret_cast<int*>(ws);
   if (cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream)) return fail_cuda("sparse_attn_fwd: status", e);
   if (S == 0) return 0;
+  // No kv rows: every slot is masked (an index must be < Nkv), so the result is
+  // the all-masked one (O = 0, LSE = sink) and nothing may be gathered.  The kv
+  // tensor map then points at q, which the kernel never reads through it.
+  if (Nkv == 0) K = 0;
 
   CUtensorMap mq, mkv;
   if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, attn::kHeads, 0)) return rc;
-  if (int rc = make_tmap_2d_16b(&mkv, Nkv1 > 0 ? kv : kv2, D, (uint64_t)B * (Nkv1 > 0 ? Nkv1 : (Nkv2 > 0 ? Nkv2 : 1)), 64, 1, 0))
+  const void* kv_map_base = Nkv1 > 0 ? kv : (Nkv2 > 0 ? kv2 : q);
+  if (int rc = make_tmap_2d_16b(&mkv, kv_map_base, D, (uint64_t)B * (Nkv1 > 0 ? Nkv1 : (Nkv2 > 0 ? Nkv2 : 1)), 64, 1, 0))
     return rc;
 
   attn::Params p{};
@@ -835,10 +867,14 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
   p.o_ld = Dv;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.idx = topk_idxs;
+  p.comp = K > 0 ? reinterpret_cast<const long long*>(comp) : nullptr;
+  p.comp_k = comp_k;
+  p.nwin = nwin;
+  p.s_off = s_off;
   p.kv = reinterpret_cast<const __nv_bfloat16*>(kv);
   p.kv2 = reinterpret_cast<const __nv_bfloat16*>(kv2);
   // two atoms per row go through TMA gathers when kv is one tensor (measured best at D=576)
-  p.na_tma = Nkv2 > 0 ? 0 : (NA >= 6 ? 2 : 0);
+  p.na_tma = (Nkv2 > 0 || Nkv == 0) ? 0 : (NA >= 6 ? 2 : 0);
   p.Nkv1 = Nkv1;
   p.sink = attn_sink;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
@@ -865,6 +901,32 @@ int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* k
     done += pass;
   }
   return 0;
+}
+
+}  // namespace si
+
+extern "C" {
+
+int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
+                           const int32_t* topk_idxs, int B, int S, int H, int D, int K, int Dv, float softmax_scale,
+                           void* o, float* lse, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  return si::run_sparse_attn(q, kv, Nkv, kv2, Nkv2, attn_sink, topk_idxs, nullptr, 0, 0, 0, B, S, H, D, K, Dv,
+                             softmax_scale, o, lse, ws, ws_bytes, stream);
+}
+
+int si_csa_sparse_attn_fwd(const void* q, const void* kv, int S_total, const void* kv_comp, int T,
+                           const float* attn_sink, const int64_t* comp_idx, int top_k, int n_win, long long s_offset,
+                           int B, int S, int H, int D, int Dv, float softmax_scale, void* o, float* lse, void* ws,
+                           size_t ws_bytes, cudaStream_t stream) {
+  using namespace si;
+  if (n_win < 0 || top_k < 0) return fail("csa_sparse_attn_fwd: n_win and top_k must be >= 0");
+  if (top_k > 0 && !comp_idx) return fail("csa_sparse_attn_fwd: null comp_idx");
+  if (s_offset < 0 || s_offset + S > S_total)
+    return fail("csa_sparse_attn_fwd: query slice [%lld, %lld) outside the sequence of %d tokens", s_offset,
+                s_offset + S, S_total);
+  if ((long long)n_win + top_k >= (1ll << 30)) return fail("csa_sparse_attn_fwd: n_win + top_k too large");
+  return run_sparse_attn(q, kv, S_total, kv_comp, T, attn_sink, nullptr, comp_idx, top_k, n_win, s_offset, B, S, H,
+                         D, n_win + top_k, Dv, softmax_scale, o, lse, ws, ws_bytes, stream);
 }
 
 int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,

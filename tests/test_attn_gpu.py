@@ -105,3 +105,47 @@ def test_q_atom_ring_many_items(B, S, H, D, K):
     q, kv, sink, idx = oracle.attn_inputs(B, S, H, D, 300, K, ratio=1, seed=D + H)
     idx[:, :, 5::7] = -1
     _check(q, kv, sink, idx)
+
+
+def test_sink_far_above_scores():
+    """A sink ~100 nats above every score: the shift is max(m, sink), so the
+    denominator stays finite; O ~ 0 and LSE ~ sink (sparse_attn_fwd.py:152-156)."""
+    q, kv, sink, idx = oracle.attn_inputs(1, 16, 64, 128, 64, 32, ratio=1, seed=7)
+    sink = torch.full((64,), 100.0)
+    sink[::2] = -100.0  # even heads: far below
+    o, ro = _check(q, kv, sink, idx)
+    assert o[..., 1::2, :].abs().max().item() < 1e-3  # odd heads carry the +100 sink
+
+
+def test_no_kv_rows_all_masked():
+    """N_kv = 0: every slot is masked, O = 0 and LSE = sink, nothing is gathered."""
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    H, D = 64, 576
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn((1, 8, H, D), generator=g).bfloat16().cuda()
+    kv = torch.empty((1, 0, D), dtype=torch.bfloat16, device="cuda")
+    sink = torch.randn(H, generator=g).cuda()
+    idx = torch.randint(0, 4, (1, 8, 16), dtype=torch.int32, device="cuda")
+    o, lse = sparse_attn_fwd(q, kv, sink, idx, d_v=512)
+    torch.cuda.synchronize()
+    assert o.abs().max().item() == 0.0
+    torch.testing.assert_close(lse, sink.view(1, 1, H).expand_as(lse), atol=1e-5, rtol=1e-5)
+
+
+def test_sparse_attn_autograd_wrapper():
+    """flash_sparse.triton.sparse_attn (triton/__init__.py:50-61): forward equals
+    sparse_attn_fwd's output; backward of an input that requires grad raises."""
+    from flash_sparse.triton import sparse_attn
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    q, kv, sink, idx = oracle.attn_inputs(1, 24, 64, 576, 128, 48, ratio=1, seed=9)
+    q, kv, sink, idx = q.cuda(), kv.cuda(), sink.cuda(), idx.cuda()
+    o_ref, _ = sparse_attn_fwd(q, kv, sink, idx, d_v=512)
+    o = sparse_attn(q, kv, sink, idx, d_v=512)
+    assert torch.equal(o, o_ref)
+    qg = q.clone().requires_grad_(True)
+    out = sparse_attn(qg, kv, sink, idx, d_v=512)
+    assert out.requires_grad
+    with pytest.raises(NotImplementedError):
+        out.float().sum().backward()

@@ -170,3 +170,91 @@ def test_flash_sparse_reference_module(golden):
     idx = oracle.build_csa_topk_idxs(scores, nw, k, 4)
     ro, _ = oracle.sparse_attn(q, torch.cat([kv, kvc], dim=1), sink, idx)
     assert (o - ro).abs().max().item() <= 2e-2
+
+
+def test_flash_csa_forward_config5_full_size_sampled_rows():
+    """BASELINE configs[4] at its own size: B=2, S=131,072, H=64, D=576/512,
+    H_I=64, D_I=128, m=4, n_win=128, top_k=512, mean-pool compressors, zero
+    sink, seed 0 (CUDA generator).  On sampled queries of both batches: the
+    compressed top-k index sets equal the oracle's up to certified fp32 ties,
+    the attention index list equals the oracle's window + compressed list, and
+    the layer output matches the oracle's attention over that list (atol 2e-2)."""
+    from streamindex_b200.csa import flash_csa_forward, mean_pool_compress
+    from streamindex_b200.indexer import chunked_indexer_topk
+    from oracle.csa import compressed_to_global
+    from topk_parity import assert_topk_exact_up_to_ties
+
+    B, S, H, D, HI, DI, m, nwin, k = 2, 131072, 64, 576, 64, 128, 4, 128, 512
+    T = S // m
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    x_kv = torch.randn((B, S, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    x_k = torch.randn((B, S, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
+    q = torch.randn((B, S, H, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
+    q_idx = torch.randn((B, S, HI, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
+    w = torch.randn((B, S, HI), generator=g, device=dev)
+    sink = torch.zeros(H, device=dev)
+    kvc, kc = mean_pool_compress(x_kv, m), mean_pool_compress(x_k, m)
+    o = flash_csa_forward(q, x_kv, kvc, q_idx, kc, w, sink, n_win=nwin, top_k=k, m=m, d_v=512)
+    comp, comp_v = chunked_indexer_topk(q_idx, kc, w, k, causal_ratio=m)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(o.float()).all())
+    # the compressors against the oracle (fp32 mean, bf16 out)
+    for b in range(B):
+        sl = slice(0, 4096)
+        ref = oracle.mean_pool_compress(x_kv[b:b + 1, : 4096 * m].cpu(), m).float()
+        assert (kvc[b:b + 1, sl].float().cpu() - ref).abs().max().item() <= 1e-2
+    kv_full_cpu = torch.cat([x_kv, kvc], dim=1).cpu()
+    kc_cpu = kc.cpu()
+    rows = [0, 3, 127, 128, 4095, 65536, 131071]
+    for b in range(B):
+        for s_ in rows:
+            qs = q_idx[b:b + 1, s_:s_ + 1].cpu()
+            ws = w[b:b + 1, s_:s_ + 1].cpu()
+            n = min(T, (s_ + 1) // m)
+            kk = min(k, n)
+            if n > 0:
+                sc = oracle.lightning_indexer(qs, kc_cpu[b:b + 1, :n], ws)
+                oi, ov = oracle.topk_desc_stable(sc, kk)
+                assert_topk_exact_up_to_ties(qs, kc_cpu[b:b + 1], ws, comp[b:b + 1, s_:s_ + 1, :kk].cpu(),
+                                             comp_v[b:b + 1, s_:s_ + 1, :kk].cpu(), oi, ov, s_rows=[0],
+                                             check_mean_recall=False)
+            assert bool((comp[b, s_, kk:] == -1).all())
+            # the attention index list the layer used: window, then the GPU's picks + S
+            gi = comp[b:b + 1, s_:s_ + 1].cpu()
+            win = oracle.sliding_window_idxs(1, s_ + 1, nwin)[:, s_:s_ + 1]
+            idx = torch.cat([win.long(), compressed_to_global(gi, S)], dim=-1).int()
+            ro, _ = oracle.sparse_attn(q[b:b + 1, s_:s_ + 1].cpu(), kv_full_cpu[b:b + 1], sink.cpu(), idx, D ** -0.5,
+                                       d_v=512)
+            assert (o[b:b + 1, s_:s_ + 1].float().cpu() - ro).abs().max().item() <= 2e-2
+
+
+def test_fused_index_build_equals_materialised_list():
+    """The CSA index list built in the attention kernel's index ring equals the
+    materialised [B,S,n_win+k] list (si_csa_build_idx, pinned to the reference
+    golden above) fed to the explicit-index kernel: bit-identical outputs, for a
+    whole sequence and for a query slice with a global offset."""
+    from streamindex_b200.attention import _attn_call, _csa_attn_call
+    from streamindex_b200.csa import csa_index_list
+    from streamindex_b200.indexer import indexer_topk_slice
+
+    B, S, H, D, HI, DI, m, nwin, k = 2, 700, 64, 576, 64, 128, 4, 48, 40
+    g = torch.Generator().manual_seed(8)
+    q = (torch.randn((B, S, H, D), generator=g) * D ** -0.5).bfloat16().cuda()
+    kv = (torch.randn((B, S, D), generator=g) * D ** -0.5).bfloat16().cuda()
+    kvc = (torch.randn((B, S // m, D), generator=g) * D ** -0.5).bfloat16().cuda()
+    q_idx = (torch.randn((B, S, HI, DI), generator=g) * DI ** -0.5).bfloat16().cuda()
+    kc = (torch.randn((B, S // m, DI), generator=g) * DI ** -0.5).bfloat16().cuda()
+    w = torch.randn((B, S, HI), generator=g).cuda()
+    sink = torch.randn(H, generator=g).cuda()
+    comp, _ = indexer_topk_slice(q_idx, kc, w, k, m, 0)
+    o_f, l_f = _csa_attn_call(q, kv, kvc, sink, comp, nwin, 0, D ** -0.5, 512)
+    o_m, l_m = _attn_call(q, kv, kvc, sink, csa_index_list(comp, nwin), D ** -0.5, 512)
+    torch.cuda.synchronize()
+    assert torch.equal(o_f, o_m) and torch.equal(l_f, l_m)
+    # slice [a, b) of the sequence: window and causality from global positions
+    a, b = 256, 640
+    cs, _ = indexer_topk_slice(q_idx[:, a:b], kc, w[:, a:b], k, m, a)
+    o_s, _ = _csa_attn_call(q[:, a:b], kv, kvc, sink, cs, nwin, a, D ** -0.5, 512)
+    assert torch.equal(o_s, o_f[:, a:b])

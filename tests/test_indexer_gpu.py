@@ -1,13 +1,16 @@
 """GPU parity: fused indexer + streaming top-k against the CPU oracle.
 
 Tolerances (north star): scores within 1e-2 relative; top-k index sets exact
-except at fp32-epsilon ties, set recall >= 0.999; valid counts exact.
+except at fp32-epsilon ties (every differing pick certified as a tie against
+float64 scores, ``tests/topk_parity.py``), set recall >= 0.999; valid counts
+exact.
 """
 
 import pytest
 import torch
 
 import oracle
+from topk_parity import assert_topk_exact_up_to_ties
 
 pytestmark = pytest.mark.gpu
 
@@ -24,47 +27,39 @@ def _run(B, S, H, D, T, k, ratio, seed=0, w_dtype=torch.float32, mask=False):
                                      causal_ratio=ratio, causal_mask=None if cm is None else cm.cuda())
     torch.cuda.synchronize()
     oi, ov = oracle.materialize_topk(q, kk, w, k, ratio=ratio, causal_mask=cm)
+    assert_topk_exact_up_to_ties(q, kk, w, gi.cpu(), gv.cpu(), oi, ov)
     return gi.cpu(), gv.cpu(), oi, ov
-
-
-def _assert_parity(gi, gv, oi, ov, min_recall=0.999):
-    assert gi.shape == oi.shape and gv.shape == ov.shape
-    assert torch.equal((gi >= 0).sum(-1), (oi >= 0).sum(-1)), "valid counts differ"
-    assert torch.equal(gi < 0, torch.isinf(gv)), "pads must be (-1, -inf)"
-    rec = oracle.set_recall(oi, gi)
-    assert float(rec.mean()) >= min_recall, float(rec.mean())
-    # the selected scores, position by position, agree within the score tolerance
-    assert oracle.score_close(gv, ov, 1e-2)
-    # sorted descending
-    assert bool((gv[..., :-1] >= gv[..., 1:]).all())
 
 
 @pytest.mark.parametrize("H,D", [(64, 128), (128, 128), (16, 64), (32, 32)])
 def test_indexer_topk_small(H, D):
-    gi, gv, oi, ov = _run(1, 300, H, D, 75, 16, ratio=4, seed=H + D)
-    _assert_parity(gi, gv, oi, ov)
+    _run(1, 300, H, D, 75, 16, ratio=4, seed=H + D)
 
 
 def test_indexer_topk_config1():
     """B=1, S=4096, H_I=64, D_I=128, T=1024, k=512, ratio 4, seed 0."""
-    gi, gv, oi, ov = _run(1, 4096, 64, 128, 1024, 512, ratio=4, seed=0)
-    _assert_parity(gi, gv, oi, ov)
+    _run(1, 4096, 64, 128, 1024, 512, ratio=4, seed=0)
+
+
+@pytest.mark.parametrize("S", [2048, 8192])
+def test_indexer_topk_v4_flash_published_parity_sizes(S):
+    """The published parity points at V4-Flash dims (S = 2048 and 8192 beside
+    config 1's 4096; benchmarks/results/2026-04-27/parity_v4_flash_indexer_final.log:6-8):
+    H_I=64, D_I=128, T=S/4, k=512, ratio 4, CPU-generated from seed 0."""
+    _run(1, S, 64, 128, S // 4, 512, ratio=4, seed=0)
 
 
 def test_indexer_topk_no_mask_and_bf16_weights():
-    gi, gv, oi, ov = _run(2, 130, 64, 128, 520, 40, ratio=None, seed=3, w_dtype=torch.bfloat16)
-    _assert_parity(gi, gv, oi, ov)
+    _run(2, 130, 64, 128, 520, 40, ratio=None, seed=3, w_dtype=torch.bfloat16)
 
 
 def test_indexer_topk_explicit_mask():
-    gi, gv, oi, ov = _run(1, 96, 64, 128, 300, 32, ratio=None, seed=4, mask=True)
-    _assert_parity(gi, gv, oi, ov)
+    _run(1, 96, 64, 128, 300, 32, ratio=None, seed=4, mask=True)
 
 
 def test_indexer_topk_k_larger_than_T_and_unaligned():
     """Reference test shape: S=47, T=73 with k > legal count (padding)."""
-    gi, gv, oi, ov = _run(1, 47, 16, 32, 73, 100, ratio=1, seed=901)
-    _assert_parity(gi, gv, oi, ov)
+    _run(1, 47, 16, 32, 73, 100, ratio=1, seed=901)
 
 
 def test_indexer_score_materialised():
@@ -79,8 +74,7 @@ def test_indexer_score_materialised():
 
 def test_indexer_topk_v4_pro_dims():
     """BASELINE config 3 dims at small S: H_I=128, top_k=1024, ratio 4."""
-    gi, gv, oi, ov = _run(1, 8192, 128, 128, 2048, 1024, ratio=4, seed=2)
-    _assert_parity(gi, gv, oi, ov)
+    _run(1, 8192, 128, 128, 2048, 1024, ratio=4, seed=2)
 
 
 def test_run_host_pipelined_matches_device_path():
@@ -100,14 +94,16 @@ def test_run_host_pipelined_matches_device_path():
         assert torch.equal(hi, di) and torch.equal(hs, dv)
 
 
-def test_full_size_config2_properties_and_sampled_rows():
-    """BASELINE configs[1] at its largest size, S=1,048,576 (T=262,144, k=512):
+@pytest.mark.parametrize("H,k", [(64, 512), (128, 1024)])
+def test_full_size_config2_properties_and_sampled_rows(H, k):
+    """BASELINE configs[1] (H_I=64, k=512) and configs[2] (V4-Pro: H_I=128,
+    k=1024) at their largest size, S=1,048,576 (T=262,144):
     size-independent properties on every row (sorted descending, indices legal
     under t < (s+1)//4 and distinct, exact valid counts min(k, (s+1)//4), pads
     -1/-inf) plus exact oracle parity on sampled rows spread over S."""
     from streamindex_b200.indexer import IndexerTopk
 
-    S, H, D, k, r = 1 << 20, 64, 128, 512, 4
+    S, D, r = 1 << 20, 128, 4
     T = S // r
     dev = torch.device("cuda")
     g = torch.Generator(device=dev)
@@ -129,19 +125,22 @@ def test_full_size_config2_properties_and_sampled_rows():
     srt, _ = torch.where(valid, idx, torch.full_like(idx, -1)).sort(dim=-1)
     dup = (srt[..., 1:] == srt[..., :-1]) & (srt[..., 1:] >= 0)
     assert not bool(dup.any())
-    # oracle on sampled rows (full key range of each)
-    rows = torch.tensor([5, 2047, 2048, 100003, 524287, 777777, S - 1])
+    # oracle on sampled rows (full key range of each): per-row recall >= 0.999
+    # unless every difference is a certified fp32 tie
+    rows = [5, 2047, 2048, 100003, 524287, 777777, S - 1]
     kc = kk.cpu()
-    for s_ in rows.tolist():
+    recalls = []
+    for s_ in rows:
         qs = q[:, s_:s_ + 1].cpu()
         ws = w[:, s_:s_ + 1].cpu()
         n = min(T, (s_ + 1) // r)
         sc_ref = oracle.lightning_indexer(qs, kc[:, :n], ws)
         oi, ov = oracle.topk_desc_stable(sc_ref, min(k, n))
-        gi = idx[0, s_, : min(k, n)].cpu()
-        gv = sc[0, s_, : min(k, n)].cpu()
-        assert float(oracle.set_recall(oi.view(1, 1, -1), gi.view(1, 1, -1))) >= 0.995
-        assert oracle.score_close(gv, ov.view(-1), 1e-2)
+        gi = idx[:, s_:s_ + 1, : min(k, n)].cpu()
+        gv = sc[:, s_:s_ + 1, : min(k, n)].cpu()
+        assert_topk_exact_up_to_ties(qs, kc, ws, gi, gv, oi, ov, s_rows=[0], check_mean_recall=False)
+        recalls.append(float(oracle.set_recall(oi, gi)))
+    assert sum(recalls) / len(recalls) >= 0.999, recalls
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -174,7 +173,7 @@ def test_indexer_score_topk_width_and_mask():
     gi, gv = si.indexer_score_topk(q.cuda(), kk.cuda(), w.cuda(), 100, causal_mask=cm.cuda())
     assert gi.shape == (1, 64, 40)
     oi, ov = oracle.materialize_topk(q, kk, w, 100, causal_mask=cm, pad=False)
-    _assert_parity(gi.cpu(), gv.cpu(), oi, ov)
+    assert_topk_exact_up_to_ties(q, kk, w, gi.cpu(), gv.cpu(), oi, ov)
 
 
 def test_indexer_fp16_operands():
@@ -184,4 +183,4 @@ def test_indexer_fp16_operands():
     q16, k16 = q.float().half(), kk.float().half()
     gi, gv = si.chunked_indexer_topk(q16.cuda(), k16.cuda(), w.cuda(), 24, causal_ratio=4)
     oi, ov = oracle.materialize_topk(q16, k16, w, 24, ratio=4)
-    _assert_parity(gi.cpu(), gv.cpu(), oi, ov)
+    assert_topk_exact_up_to_ties(q16, k16, w, gi.cpu(), gv.cpu(), oi, ov)

@@ -80,3 +80,34 @@ def test_gated_compressor_matches_reference(golden):
     z0 = torch.zeros_like(d["z"])
     torch.testing.assert_close(oracle.token_compressor(d["c"], z0, torch.zeros_like(d["b"]), d["m"]),
                                oracle.mean_pool_compress(d["c"], d["m"]), rtol=1e-6, atol=1e-6)
+
+
+def test_tie_certificate_accepts_ties_and_rejects_a_dropped_winner():
+    """The top-k parity rule used by the GPU tests: an fp32 reordering passes,
+    one clear winner swapped for a loser fails even in one row of many."""
+    import sys, os
+    sys.path.insert(0, os.path.dirname(__file__))
+    from topk_parity import assert_topk_exact_up_to_ties
+
+    q, k, w = oracle.indexer_inputs(1, 512, 64, 128, 128, seed=5)
+    oi, ov = oracle.materialize_topk(q, k, w, 16, ratio=4)
+    # a candidate ranked by float64 scores (another rounding) passes
+    sc64 = (torch.einsum("bshd,btd->bsht", q.double(), k.double()).clamp_min(0) * w.double()[..., None]).sum(2)
+    legal = torch.arange(128).view(1, 1, -1) < ((torch.arange(512) + 1) // 4).view(1, -1, 1)
+    ci, cv = oracle.topk_desc_stable(sc64.masked_fill(~legal, float("-inf")), 16)
+    ci = torch.where(torch.isinf(cv), torch.full_like(ci, -1), ci)
+    assert_topk_exact_up_to_ties(q, k, w, ci, cv.float(), oi, ov)
+    # swap the best pick of one row for its best non-pick: must fail
+    bad_i, bad_v = oi.clone(), ov.clone()
+    s = 400
+    sc = oracle.lightning_indexer(q[:, s:s + 1], k, w[:, s:s + 1])[0, 0]
+    lim = (s + 1) // 4
+    order = torch.sort(sc[:lim], descending=True, stable=True).indices
+    loser = int(order[16])
+    bad_i[0, s] = torch.cat([bad_i[0, s, 1:], torch.tensor([loser])])
+    bad_v[0, s] = torch.cat([bad_v[0, s, 1:], sc[loser:loser + 1]])
+    try:
+        assert_topk_exact_up_to_ties(q, k, w, bad_i, bad_v, oi, ov)
+    except AssertionError:
+        return
+    raise AssertionError("a dropped winner passed the tie certificate")
