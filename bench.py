@@ -466,10 +466,18 @@ def run_attn(a):
     tf_peak = peaks.get("bf16_tflops", 1590.0)
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     tf = flops / (ms * 1e-3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "sparse_attn_traffic.json")) as f:
+            tr = json.load(f)
+        if (H, K) == (tr["H"], tr["K"]):
+            traffic = tr["bytes_per_query"] * S  # ncu capture at S=4096 scaled by the queries of a launch
+    except Exception:
+        pass
     # CPU oracle on a small sample of the same queries
     import oracle
     torch.set_num_threads(os.cpu_count() or 1)
-    n = 8
+    n = 2048
     pos = torch.linspace(0, S - 1, n).long()
     t = time.perf_counter()
     oracle.sparse_attn(q[:, pos.to(device)].cpu(), kv.cpu(), sink.cpu(), idx[:, pos.to(device)].cpu(), D ** -0.5,
@@ -484,7 +492,7 @@ def run_attn(a):
                    "valid_slots": V, "l2": "q/o larger than L2; kv (18.9 MB) L2-resident by design"},
         "gpu_launches": a.steps,
         "roofline": {"bound": "tensor", "achieved": tf, "peak": tf_peak, "unit": "TFLOP/s", "frac": tf / tf_peak,
-                     "peak_source": "of measured (bf16_tflops burst, MEASURED_PEAKS.json)", "traffic": None,
+                     "peak_source": "of measured (bf16_tflops burst, MEASURED_PEAKS.json)", "traffic": traffic,
                      "hbm_unique_gbs": uniq / (ms * 1e-3) / 1e9, "hbm_frac": uniq / (ms * 1e-3) / 1e9 / hbm_peak,
                      "gather_gbs_from_l2": gather_bytes / (ms * 1e-3) / 1e9},
         "cpu_baseline": {"value": n / cpu_s / 1e6, "unit": "Mqueries/s", "cores": os.cpu_count(), "kind": "port",
@@ -719,7 +727,7 @@ def run_csa_e2e(a, q, q_idx, w, x_kv, x_k, sink, dev, chunk=8192):
                     "chunk c+1 and D2H of chunk c-1's output overlapped with csa_forward_slice on chunk c"}
 
 
-def run_csa_cpu(q, q_idx, w, x_kv, x_k, sink, m, nwin, k, n=6):
+def run_csa_cpu(q, q_idx, w, x_kv, x_k, sink, m, nwin, k, n=384):
     """The reference's CSA forward (oracle restatement of flash_sparse/csa.py:86-207) on n sampled queries of
     batch 0: compressors over the whole sequence, materialised indexer scores over all compressed keys, mask,
     top-k, window + compressed index list, sparse attention."""
