@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--no-gather", action="store_true")
     ap.add_argument("--attn-heads", type=int, default=64, help="attention workload: query heads (64; 128 = V4-Pro)")
     ap.add_argument("--attn-k", type=int, default=512, help="attention workload: selected kv rows per query")
+    ap.add_argument("--attn-dv", type=int, default=512, help="attention workload: value width (576 = full D)")
+    ap.add_argument("--kv-fp8", action="store_true",
+                    help="attention workload: kv stored as FP8 rows (e4m3 NoPE + fp32 block scales + bf16 RoPE)")
     ap.add_argument("--workload", default="indexer", choices=["indexer", "attn", "csa"],
                     help="indexer: the headline metric (default); attn: benchmark configs[3] sparse attention")
     return ap.parse_args()
@@ -425,7 +428,7 @@ def run_attn(a):
     """benchmark configs[3]: sparse attention forward, B=1, S=65536, H=64, D=576/512, N_kv=16384, K=512."""
     from streamindex_b200 import _lib
 
-    S, H, D, DV, NKV, K = a.S, a.attn_heads, 576, 512, 16384, a.attn_k
+    S, H, D, DV, NKV, K = a.S, a.attn_heads, 576, a.attn_dv, 16384, a.attn_k
     device = torch.device("cuda", 0)
     g = torch.Generator(device=device)
     g.manual_seed(0)
@@ -439,9 +442,22 @@ def run_attn(a):
     lib = _lib.load()
     st = _lib.stream_handle(device)
 
-    def step():
-        _lib.check(lib.si_sparse_attn_fwd(q.data_ptr(), kv.data_ptr(), sink.data_ptr(), idx.data_ptr(), 1, S, H, D,
-                                          NKV, K, DV, D ** -0.5, o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, st))
+    row_bytes = 2 * D
+    if a.kv_fp8:
+        from streamindex_b200.attention import quantize_kv_fp8
+
+        kv_rows = quantize_kv_fp8(kv, 512)  # the KV cache as stored (quantised once, outside the timed region)
+        row_bytes = kv_rows.shape[-1]
+
+        def step():
+            _lib.check(lib.si_sparse_attn_fwd_fp8kv(q.data_ptr(), kv_rows.data_ptr(), NKV, None, 0, 512,
+                                                    sink.data_ptr(), idx.data_ptr(), 1, S, H, D, K, DV, D ** -0.5,
+                                                    o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, st))
+    else:
+        def step():
+            _lib.check(lib.si_sparse_attn_fwd(q.data_ptr(), kv.data_ptr(), sink.data_ptr(), idx.data_ptr(), 1, S, H,
+                                              D, NKV, K, DV, D ** -0.5, o.data_ptr(), lse.data_ptr(), ws.data_ptr(),
+                                              256, st))
 
     for _ in range(a.warmup):
         step()
@@ -459,7 +475,7 @@ def run_attn(a):
     ms = t0.elapsed_time(t1) / a.steps
     V = int((idx >= 0).sum().item())
     flops = 2.0 * H * V * (D + DV)
-    gather_bytes = V * D * 2
+    gather_bytes = V * row_bytes
     uniq = q.numel() * 2 + o.numel() * 2 + idx.numel() * 4 + kv.numel() * 2 + lse.numel() * 4
     peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
         os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
@@ -470,7 +486,7 @@ def run_attn(a):
     try:
         with open(os.path.join(ROOT, "profiles", "sparse_attn_traffic.json")) as f:
             tr = json.load(f)
-        if (H, K) == (tr["H"], tr["K"]):
+        if (H, K, DV) == (tr["H"], tr["K"], tr["Dv"]) and not a.kv_fp8:
             traffic = tr["bytes_per_query"] * S  # ncu capture at S=4096 scaled by the queries of a launch
     except Exception:
         pass
@@ -488,7 +504,9 @@ def run_attn(a):
         "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; causal uniform indices without replacement)",
-        "config": {"workload": "sparse_attn_fwd B=1 S=%d H=%d D_qk=576 D_v=512 N_kv=16384 K=%d" % (S, H, K),
+        "config": {"workload": "sparse_attn_fwd%s B=1 S=%d H=%d D_qk=576 D_v=%d N_kv=16384 K=%d" % (
+                       "_fp8kv" if a.kv_fp8 else "", S, H, DV, K),
+                   "kv_row_bytes": row_bytes,
                    "valid_slots": V, "l2": "q/o larger than L2; kv (18.9 MB) L2-resident by design"},
         "gpu_launches": a.steps,
         "roofline": {"bound": "tensor", "achieved": tf, "peak": tf_peak, "unit": "TFLOP/s", "frac": tf / tf_peak,

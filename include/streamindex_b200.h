@@ -134,6 +134,30 @@ SI_API int si_sparse_attn_fwd_kv2(const void* q, const void* kv, int Nkv, const 
                                   int Dv, float softmax_scale, void* o, float* lse, void* ws, size_t ws_bytes,
                                   cudaStream_t stream);
 
+/* FP8 KV row format (the V4 production KV row, described in the reference's
+ * docs/ir_analysis.md:45-55; its quantisation is the reference's
+ * act_quant_simulate, flash_sparse/utils/quantization.py:19-36, at block 64):
+ *   [n_nope e4m3 | n_nope/64 fp32 block scales | pad to 16 B | D-n_nope bf16 | pad to 16 B]
+ * n_nope a multiple of 64 in [64,512], 0 < D - n_nope <= 64.  672 bytes per
+ * row at D=576/n_nope=512 (vs 1152 in bf16); 608 at the V4-Pro 512/448 split.
+ * si_fp8_kv_row_bytes returns the row size (-1 for an unsupported split). */
+SI_API int si_fp8_kv_row_bytes(int D, int n_nope);
+/* bf16 kv [rows, D] -> FP8 rows [rows, row_bytes].  Per 64-dim block:
+ * amax = max(max|x|, 1e-4), scale = bf16(amax/448), e = e4m3(clamp(bf16(x/scale), +-448)),
+ * evaluated in bf16 like the simulation, so bf16(float(e) * scale) equals
+ * act_quant_simulate(kv[..., :n_nope], 64) exactly. */
+SI_API int si_kv_quant_fp8(const void* kv, long long rows, int D, int n_nope, void* out, cudaStream_t stream);
+/* si_sparse_attn_fwd_kv2 over FP8 KV rows (kv2_rows / Nkv2 optional, same
+ * format): the gather dequantises each selected row, value = bf16(float(e) *
+ * scale), into the bf16 tile the tensor cores read, so the result equals
+ * sparse attention over the dequantised kv (the reference's FP8 simulation
+ * path, flash_sparse/reference.py:44-130 on act_quant_simulate(kv)) while each
+ * gathered row moves row_bytes instead of 2*D bytes.  q and o stay bf16. */
+SI_API int si_sparse_attn_fwd_fp8kv(const void* q, const void* kv_rows, int Nkv, const void* kv2_rows, int Nkv2,
+                                    int n_nope, const float* attn_sink, const int32_t* topk_idxs, int B, int S, int H,
+                                    int D, int K, int Dv, float softmax_scale, void* o, float* lse, void* ws,
+                                    size_t ws_bytes, cudaStream_t stream);
+
 /* CSA sparse attention with the index list built inside the kernel.
  * Replaces the index concatenation of flash_csa_forward
  * (flash_sparse/csa.py:176-179, window of flash_sparse/reference.py:460-475)

@@ -42,6 +42,11 @@ SIGNATURES = {
     "si_csa_sparse_attn_fwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
                                        ctypes.c_longlong, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
                                        c_void_p, c_void_p, c_size_t, c_void_p]),
+    "si_fp8_kv_row_bytes": (c_int, [c_int, c_int]),
+    "si_kv_quant_fp8": (c_int, [c_void_p, ctypes.c_longlong, c_int, c_int, c_void_p, c_void_p]),
+    "si_sparse_attn_fwd_fp8kv": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                         c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p,
+                                         c_void_p, c_size_t, c_void_p]),
     "si_scores_topk_ws_bytes": (c_size_t, [c_int, c_int, c_int]),
     "si_scores_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
                                c_void_p]),

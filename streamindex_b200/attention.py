@@ -115,6 +115,66 @@ def sparse_attn_fwd(
     return _attn_call(q, kv, None, attn_sink, topk_idxs, softmax_scale, dv)
 
 
+def fp8_kv_row_bytes(D: int, n_nope: int) -> int:
+    """Bytes per FP8 KV row (``[n_nope e4m3 | fp32 block scales | bf16 rope]``, 16-byte padded)."""
+    n = _lib.load().si_fp8_kv_row_bytes(int(D), int(n_nope))
+    if n < 0:
+        raise ValueError(f"unsupported FP8 row split D={D}, n_nope={n_nope}")
+    return n
+
+
+def quantize_kv_fp8(kv: torch.Tensor, n_nope: int = 512) -> torch.Tensor:
+    """bf16 kv ``[..., D]`` -> FP8 rows ``[..., row_bytes]`` uint8 (e4m3 NoPE dims with one
+    fp32 scale per 64 dims, bf16 RoPE dims).  Dequantised values equal the
+    reference's ``act_quant_simulate(kv[..., :n_nope], 64)`` (``flash_sparse/utils/quantization.py:19-36``)."""
+    assert kv.is_cuda and kv.dtype == torch.bfloat16, "kv must be a bf16 CUDA tensor"
+    D = kv.shape[-1]
+    if not (n_nope % 64 == 0 and 64 <= n_nope <= 512 and 0 < D - n_nope <= 64 and D % 8 == 0):
+        raise ValueError(f"unsupported FP8 row split D={D}, n_nope={n_nope}")
+    rb = fp8_kv_row_bytes(D, n_nope)
+    x = kv.contiguous()
+    rows = x.numel() // D
+    out = torch.empty((*kv.shape[:-1], rb), dtype=torch.uint8, device=kv.device)
+    with torch.cuda.device(kv.device):
+        _lib.check(_lib.load().si_kv_quant_fp8(x.data_ptr(), rows, D, int(n_nope), out.data_ptr(),
+                                               _lib.stream_handle(kv.device)))
+    return out
+
+
+def sparse_attn_fwd_fp8kv(q: torch.Tensor, kv_rows: torch.Tensor, n_nope: int, attn_sink: torch.Tensor,
+                          topk_idxs: torch.Tensor, softmax_scale: Optional[float] = None, *,
+                          d_v: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Sparse attention over FP8 KV rows (from :func:`quantize_kv_fp8`).
+
+    Same contract as :func:`sparse_attn_fwd` with ``kv`` replaced by its FP8
+    rows: the result equals ``sparse_attn_fwd`` over the dequantised kv."""
+    assert q.is_cuda and kv_rows.is_cuda and q.dtype == torch.bfloat16 and kv_rows.dtype == torch.uint8
+    B, S, H, D = q.shape
+    rb = fp8_kv_row_bytes(D, n_nope)
+    assert kv_rows.dim() == 3 and kv_rows.shape[0] == B and kv_rows.shape[2] == rb, "kv_rows must be [B, N_kv, row_bytes]"
+    assert attn_sink.shape == (H,) and topk_idxs.shape[:2] == (B, S)
+    K = topk_idxs.shape[-1]
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    dv = D if d_v is None else int(d_v)
+    if dv % 64:
+        raise ValueError(f"d_v ({dv}) must be a multiple of 64 for FP8 rows")
+    dev = q.device
+    qk, kvk = q.contiguous(), kv_rows.contiguous()
+    idx = topk_idxs.to(device=dev, dtype=torch.int32).contiguous()
+    sink = attn_sink.to(device=dev, dtype=torch.float32).contiguous()
+    o = torch.empty((B, S, H, dv), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, S, H), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        ws = torch.empty(256, dtype=torch.uint8, device=dev)
+        _lib.check(_lib.load().si_sparse_attn_fwd_fp8kv(
+            qk.data_ptr(), kvk.data_ptr(), kvk.shape[1], None, 0, int(n_nope), sink.data_ptr(),
+            idx.data_ptr() if K > 0 else None, B, S, H, D, K, dv, float(softmax_scale), o.data_ptr(), lse.data_ptr(),
+            ws.data_ptr(), 256, _lib.stream_handle(dev)))
+        _lib.maybe_check_status(ws, dev, "sparse_attn_fwd_fp8kv")
+    return o, lse
+
+
 class _SparseAttnFunc(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, kv, attn_sink, topk_idxs, softmax_scale, d_v):

@@ -37,6 +37,7 @@
 // memory, so no gather thread waits on a global load of an index), warps 17-20
 // move the staged Q atoms into TMEM.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "capi_common.h"
 #include "ptx.cuh"
@@ -54,6 +55,16 @@ constexpr int kMaxAtoms = 16;  // D <= 1024
 constexpr int kQStage = 4;     // Q staging atoms (64 rows x 128 B) in shared memory
 constexpr int kQCol = 64;      // first TMEM column of Q (lanes 16-31 of each quarter), after the two S buffers
 constexpr int kQSlots = (512 - kQCol) / 32;  // 32-column Q atom slots in TMEM (14)
+// Full-width value output in one pass (the reference's default D_v = D = 576 of
+// the 576/512 MLA layout): O's first 512 columns stay in lanes 0-15, the extra
+// kXV value columns take the last kXV TMEM columns of lanes 16-31 (after S and
+// a Q ring shortened to kQSlotsXV slots, so D <= 768 there).
+constexpr int kXV = 64;
+constexpr int kQSlotsXV = (512 - kQCol - kXV) / 32;  // 12
+template <int XV>
+struct QRing {
+  static constexpr int kSlots = XV ? kQSlotsXV : kQSlots;
+};
 
 // Q lives in tensor memory as the A operand of Q.K^T.  Its atoms fill a ring
 // of kQSlots 32-column slots: item j's atom a (CTA-local numbering) goes to
@@ -89,6 +100,11 @@ struct Params {
   int hgroups;         // ceil(H/64)
   int na_tma;          // leading atoms of each kv row gathered by TMA (warp 14); the rest by cp.async
   int o_v8;            // o rows are 32-byte aligned: 256-bit output stores
+  // FP8 KV rows (fp8 != 0): kv / kv2 hold rows of row_bytes bytes:
+  //   [n_nope e4m3 | n_nope/64 fp32 block scales | pad to 16 B | n_rope bf16 (at rope_off) | pad to 16 B]
+  // dequantised by the gather warps into the same bf16 stage layout:
+  //   value = bf16(float(e4m3) * scale[block])
+  int fp8, n_nope, row_bytes, rope_off;
   unsigned long long* trace;  // debug builds (SI_ATTN_TRACE) only: per-role timestamps of CTA 0
 };
 
@@ -153,8 +169,37 @@ __device__ __forceinline__ const __nv_bfloat16* kv_row_ptr(const Params& p, int 
   if (v < p.Nkv1) return p.kv + ((size_t)b * p.Nkv1 + v) * p.D;
   return p.kv2 + ((size_t)b * (p.Nkv - p.Nkv1) + (v - p.Nkv1)) * p.D;
 }
+__device__ __forceinline__ const uint8_t* kv_row_ptr_fp8(const Params& p, int b, int v) {
+  if (v < p.Nkv1) return reinterpret_cast<const uint8_t*>(p.kv) + ((size_t)b * p.Nkv1 + v) * p.row_bytes;
+  return reinterpret_cast<const uint8_t*>(p.kv2) + ((size_t)b * (p.Nkv - p.Nkv1) + (v - p.Nkv1)) * p.row_bytes;
+}
 
-template <int NK, int DVH>
+// 16 e4m3 values -> 16 bf16 = bf16(float(e) * scale), two 16-byte stage chunks.
+__device__ __forceinline__ void dequant16_e4m3(const uint4& x, float scale, uint4& lo, uint4& hi) {
+  const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+  uint32_t out[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t h01, h23;  // f16x2 (exact: every e4m3 value is an f16 value)
+    asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+        : "=r"(h01), "=r"(h23) : "r"(w[i]));
+    const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+    const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+    out[2 * i] = pack_bf16x2(f01.x * scale, f01.y * scale);
+    out[2 * i + 1] = pack_bf16x2(f23.x * scale, f23.y * scale);
+  }
+  lo = make_uint4(out[0], out[1], out[2], out[3]);
+  hi = make_uint4(out[4], out[5], out[6], out[7]);
+}
+
+// 128-byte-swizzled stage offset of 16-byte chunk ch of row r in atom a.
+template <int NK>
+__device__ __forceinline__ uint32_t stage_off(int a, int r, int ch) {
+  return (uint32_t)(a * NK * 128 + r * 128) + ((uint32_t)(ch ^ (r & 7)) << 4);
+}
+
+template <int NK, int DVH, int XV>
 __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t* sP, uint32_t tmem, int warp,
                                              uint32_t lane, int nitems, int ntiles) {
   constexpr float kLn2 = 0.6931471805599453f;
@@ -290,6 +335,13 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
           for (int j = 0; j < 32; ++j) v[j] *= alpha;
           tmem_st16x32bx2_x32<DVH>(tq + c * 32, v);
         }
+        if (XV) {  // extra value columns in lanes 16-31: this thread's 32 of them
+          float v[32];
+          tmem_ld16x32bx2_x32_sync<XV / 2>(tq + (16u << 16) + (512 - XV), v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= alpha;
+          tmem_st16x32bx2_x32<XV / 2>(tq + (16u << 16) + (512 - XV), v);
+        }
         tmem_st_wait();
       }
       {
@@ -328,15 +380,21 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
     if (half == 0 && head < p.H && p.lse)
       p.lse[(size_t)bs * p.H + head] = l_tot > 0.f ? (m_fin + log2f(l_tot)) * kLn2 : -1.0e30f;
     __nv_bfloat16* orow = p.o + ((size_t)bs * p.H + head) * p.o_ld + p.o_off + half * DVH;
+    constexpr int NC = DVH / 32 + (XV ? 1 : 0);
 #pragma unroll 1
-    for (int c = 0; c < DVH / 32; ++c) {
+    for (int c = 0; c < NC; ++c) {
       float v[32];
-      tmem_ld16x32bx2_x32_sync<DVH>(tq + c * 32, v);
+      __nv_bfloat16* dst = orow + c * 32;
+      if (XV && c == DVH / 32) {  // the extra value columns (lanes 16-31)
+        tmem_ld16x32bx2_x32_sync<XV / 2>(tq + (16u << 16) + (512 - XV), v);
+        dst = orow - half * DVH + 2 * DVH + half * (XV / 2);
+      } else {
+        tmem_ld16x32bx2_x32_sync<DVH>(tq + c * 32, v);
+      }
       if (head < p.H) {
         uint32_t w[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j] * inv, v[2 * j + 1] * inv);
-        __nv_bfloat16* dst = orow + c * 32;
         if (p.o_v8) {  // two 32-byte stores: half the store transactions of 16-byte ones
 #pragma unroll
           for (int j = 0; j < 16; j += 8)
@@ -357,7 +415,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
   }
 }
 
-template <int NK, int DVH>
+template <int NK, int DVH, int XV>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
                            Params p) {
@@ -365,6 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int DV = 2 * DVH;
   constexpr int NMMA = DV < 256 ? DV : 256;  // UMMA N of the PV product
   constexpr int NCH = DV / NMMA;
+  constexpr int QSL = QRing<XV>::kSlots;  // Q atom slots in TMEM
+  static_assert(XV == 0 || DV == 512, "extra value columns only beside a full 512-column O");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NA = p.NA;
@@ -481,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++jj) {
         for (int a = 0; a < NA; ++a) {
           const int g = jj * NA + a;
-          const int prev = g - kQSlots;  // atom that last used this slot
+          const int prev = g - QSL;  // atom that last used this slot
           if (prev >= 0 && !wait_items_done(prev / NA + 1)) {
             ok = false;
             break;
@@ -502,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             v[4 * k + 2] = x.z;
             v[4 * k + 3] = x.w;
           }
-          tmem_st16x32bx2_x16<16>(tq + (uint32_t)(g % kQSlots) * 32, v);
+          tmem_st16x32bx2_x16<16>(tq + (uint32_t)(g % QSL) * 32, v);
           __syncwarp();
           if (lane == 0) mbar_arrive(&ms->qs_empty[qslot]);
           if (++qslot == (uint32_t)kQStage) {
@@ -657,6 +717,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         SI_TRACE_IF(tr, 0, ii, t, 1);
+        if (p.fp8) {
+          // FP8 rows: this thread loads 16-byte chunks q = c + 8i of the row's
+          // e4m3 part (64-dim block q/4 = atom q/4), the row's block scales and
+          // rope chunk c, then writes the dequantised bf16 chunks into the stage.
+          uint4 x[4] = {}, rp = make_uint4(0u, 0u, 0u, 0u);
+          float4 sc0 = make_float4(0.f, 0.f, 0.f, 0.f), sc1 = sc0;
+          const int nq = p.n_nope >> 4;
+          if (vld) {
+            const uint8_t* rowp = kv_row_ptr_fp8(p, b, row);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int qc = (int)c + 8 * i;
+              if (qc < nq) x[i] = __ldg(reinterpret_cast<const uint4*>(rowp) + qc);
+            }
+            sc0 = __ldg(reinterpret_cast<const float4*>(rowp + p.n_nope));
+            if (p.n_nope > 256) sc1 = __ldg(reinterpret_cast<const float4*>(rowp + p.n_nope) + 1);
+            if ((int)c * 8 < p.D - p.n_nope) rp = __ldg(reinterpret_cast<const uint4*>(rowp + p.rope_off) + c);
+          }
+          uint8_t* stg = sKV + (size_t)st * SB;
+          const float scs[8] = {sc0.x, sc0.y, sc0.z, sc0.w, sc1.x, sc1.y, sc1.z, sc1.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int qc = (int)c + 8 * i;
+            if (qc < nq) {
+              uint4 lo, hi;
+              // block qc/4 = 2i + (c >= 4): static indices, no local-memory array
+              dequant16_e4m3(x[i], (c >= 4) ? scs[2 * i + 1] : scs[2 * i], lo, hi);
+              const int a = qc >> 2, ch = 2 * (qc & 3);
+              *reinterpret_cast<uint4*>(stg + stage_off<NK>(a, r, ch)) = lo;
+              *reinterpret_cast<uint4*>(stg + stage_off<NK>(a, r, ch + 1)) = hi;
+            }
+          }
+          *reinterpret_cast<uint4*>(stg + stage_off<NK>(p.n_nope >> 6, r, (int)c)) = rp;
+          fence_proxy_async_smem();
+          mbar_arrive(&ms->kv_full[st]);
+          if (++st == (uint32_t)NST) {
+            st = 0;
+            kph ^= 1;
+          }
+          continue;
+        }
         const uint32_t base = smem_u32(sKV + (size_t)st * SB) + dst_off;
         const __nv_bfloat16* src = (vld ? kv_row_ptr(p, b, row) : p.kv) + c * 8;
 #pragma unroll
@@ -708,7 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t d_s = tmem + (16u << 16) + (t & 1) * NK;
           const uint32_t a_q = tmem + (16u << 16) + kQCol;
           for (int a = 0; a < NA; ++a) {
-            const uint32_t a_col = a_q + (uint32_t)((jj * NA + a) % kQSlots) * 32;
+            const uint32_t a_col = a_q + (uint32_t)((jj * NA + a) % QSL) * 32;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               umma_f16_tmem_a(d_s, a_col + kk * 8, umma_desc_sw128(kvbase + a * NK * 128 + kk * 32), idesc1,
@@ -731,6 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // softmax published P, so this commit covers every read of the stage.
     if (lane == 0) {
       const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, 1) | (1u << 16);  // B (V) MN-major
+      const uint32_t idesc2x = umma_idesc_f16(kHeads, XV ? XV : 64, 1) | (1u << 16);
       uint32_t st = 0, pf[2] = {0, 0}, ofr = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
@@ -762,6 +864,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t bdesc = umma_desc(vbase + nh * (NMMA / 64) * NK * 128 + kk * 2048, NK * 128, 1024, 2);
               umma_f16(tmem + nh * NMMA, adesc, bdesc, idesc2, (j > 0 || kk > 0) ? 1u : 0u);
             }
+            if (XV) {  // value columns [DV, DV+XV) into lanes 16-31
+              const uint64_t bdesc = umma_desc(vbase + (DV / 64) * NK * 128 + kk * 2048, NK * 128, 1024, 2);
+              umma_f16(tmem + (16u << 16) + (512 - XV), adesc, bdesc, idesc2x, (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&ms->pv_done[j & 1]);
           umma_commit(&ms->kv_empty[st]);
@@ -771,7 +877,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    attn_softmax<NK, DVH>(p, ms, sP, tmem, warp, lane, nitems, ntiles);
+    attn_softmax<NK, DVH, XV>(p, ms, sP, tmem, warp, lane, nitems, ntiles);
   }
 
   tc_fence_before();
@@ -790,15 +896,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 namespace si {
 namespace attn {
 
-template <int DVH>
+template <int DVH, int XV = 0>
 static cudaError_t launch_t(const CUtensorMap& mq, const CUtensorMap& mkv, const Params& p, int grid,
                             cudaStream_t stream) {
   constexpr int NK = 32;
   static unsigned long long configured = 0;  // devices on which the attribute is set
-  cudaError_t e = set_smem_attr_once(reinterpret_cast<const void*>(sparse_attn_fwd_kernel<NK, DVH>), kSmemMax,
+  cudaError_t e = set_smem_attr_once(reinterpret_cast<const void*>(sparse_attn_fwd_kernel<NK, DVH, XV>), kSmemMax,
                                      &configured);
   if (e != cudaSuccess) return e;
-  sparse_attn_fwd_kernel<NK, DVH><<<grid, kThreads, smem_bytes<NK>(p.NA), stream>>>(mq, mkv, p);
+  sparse_attn_fwd_kernel<NK, DVH, XV><<<grid, kThreads, smem_bytes<NK>(p.NA), stream>>>(mq, mkv, p);
   return cudaGetLastError();
 }
 
@@ -809,6 +915,7 @@ static cudaError_t launch(const CUtensorMap& mq, const CUtensorMap& mkv, const P
     case 128: return launch_t<64>(mq, mkv, p, grid, stream);
     case 256: return launch_t<128>(mq, mkv, p, grid, stream);
     case 512: return launch_t<256>(mq, mkv, p, grid, stream);
+    case 512 + kXV: return launch_t<256, kXV>(mq, mkv, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -826,10 +933,22 @@ extern "C" {
 }  // extern "C"
 
 namespace si {
+// Byte layout of one FP8 KV row (see Params::fp8).
+struct Fp8RowLayout {
+  int n_nope, rope_off, row_bytes;
+};
+static inline Fp8RowLayout fp8_row_layout(int D, int n_nope) {
+  Fp8RowLayout l;
+  l.n_nope = n_nope;
+  l.rope_off = ((n_nope + 4 * (n_nope / 64)) + 15) / 16 * 16;
+  l.row_bytes = ((l.rope_off + 2 * (D - n_nope)) + 15) / 16 * 16;
+  return l;
+}
+
 static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
                            const int32_t* topk_idxs, const int64_t* comp, int comp_k, int nwin, long long s_off,
                            int B, int S, int H, int D, int K, int Dv, float softmax_scale, void* o, float* lse,
-                           void* ws, size_t ws_bytes, cudaStream_t stream) {
+                           void* ws, size_t ws_bytes, cudaStream_t stream, int fp8_n_nope = 0) {
   if (Nkv2 < 0 || (Nkv2 > 0 && !kv2)) return fail("sparse_attn_fwd: bad second kv tensor");
   if (Nkv2 > 0 && (((uintptr_t)kv2) & 15)) return fail("sparse_attn_fwd: 16-byte alignment of kv2");
   const int Nkv1 = Nkv;
@@ -858,8 +977,16 @@ static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* k
 
   CUtensorMap mq, mkv;
   if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, attn::kHeads, 0)) return rc;
-  const void* kv_map_base = Nkv1 > 0 ? kv : (Nkv2 > 0 ? kv2 : q);
-  if (int rc = make_tmap_2d_16b(&mkv, kv_map_base, D, (uint64_t)B * (Nkv1 > 0 ? Nkv1 : (Nkv2 > 0 ? Nkv2 : 1)), 64, 1, 0))
+  if (fp8_n_nope) {
+    if (fp8_n_nope % 64 || fp8_n_nope > 512 || D - fp8_n_nope <= 0 || D - fp8_n_nope > 64 || D % 8)
+      return fail("sparse_attn_fwd_fp8kv: need n_nope a multiple of 64 in [64,512] and 0 < D - n_nope <= 64, "
+                  "D %% 8 == 0 (got D=%d, n_nope=%d)", D, fp8_n_nope);
+  }
+  // FP8 rows are not bf16 tensors: the kv map (used only by TMA row gathers,
+  // which are off for FP8 rows) then points at q like the empty-kv case.
+  const void* kv_map_base = fp8_n_nope ? q : (Nkv1 > 0 ? kv : (Nkv2 > 0 ? kv2 : q));
+  if (int rc = make_tmap_2d_16b(&mkv, kv_map_base, D,
+                                (uint64_t)(fp8_n_nope ? 1 : B * (Nkv1 > 0 ? Nkv1 : (Nkv2 > 0 ? Nkv2 : 1))), 64, 1, 0))
     return rc;
 
   attn::Params p{};
@@ -874,7 +1001,14 @@ static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* k
   p.kv = reinterpret_cast<const __nv_bfloat16*>(kv);
   p.kv2 = reinterpret_cast<const __nv_bfloat16*>(kv2);
   // two atoms per row go through TMA gathers when kv is one tensor (measured best at D=576)
-  p.na_tma = (Nkv2 > 0 || Nkv == 0) ? 0 : (NA >= 6 ? 2 : 0);
+  p.na_tma = (Nkv2 > 0 || Nkv == 0 || fp8_n_nope) ? 0 : (NA >= 6 ? 2 : 0);
+  if (fp8_n_nope) {
+    const Fp8RowLayout l = fp8_row_layout(D, fp8_n_nope);
+    p.fp8 = 1;
+    p.n_nope = l.n_nope;
+    p.rope_off = l.rope_off;
+    p.row_bytes = l.row_bytes;
+  }
   p.Nkv1 = Nkv1;
   p.sink = attn_sink;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
@@ -887,7 +1021,17 @@ static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* k
   const long long items = (long long)B * S * p.hgroups;
   const int sms = device_sm_count();
   const int grid = (int)(items < sms ? items : sms);
-  // value columns in passes of 512 / 256 / 128 / 64 (TMEM holds at most 512 fp32 columns)
+  if (Dv == 512 + attn::kXV && NA <= attn::kQSlotsXV) {
+    // full 576-wide output in one pass: O = 512 columns in lanes 0-15 + 64 in lanes 16-31
+    p.Dv = Dv;
+    p.dv_off = 0;
+    p.o_off = 0;
+    p.lse = lse;
+    cudaError_t e = attn::launch(mq, mkv, p, grid, stream);
+    if (e != cudaSuccess) return fail_cuda("sparse_attn_fwd: kernel launch", e);
+    return 0;
+  }
+  // other widths: value columns in passes of 512 / 256 / 128 / 64 (TMEM holds at most 512 fp32 columns)
   int done = 0;
   while (done < Dv) {
     int pass = 512;
@@ -927,6 +1071,20 @@ int si_csa_sparse_attn_fwd(const void* q, const void* kv, int S_total, const voi
   if ((long long)n_win + top_k >= (1ll << 30)) return fail("csa_sparse_attn_fwd: n_win + top_k too large");
   return run_sparse_attn(q, kv, S_total, kv_comp, T, attn_sink, nullptr, comp_idx, top_k, n_win, s_offset, B, S, H,
                          D, n_win + top_k, Dv, softmax_scale, o, lse, ws, ws_bytes, stream);
+}
+
+int si_fp8_kv_row_bytes(int D, int n_nope) {
+  if (n_nope <= 0 || n_nope % 64 || D <= n_nope) return -1;
+  return si::fp8_row_layout(D, n_nope).row_bytes;
+}
+
+int si_sparse_attn_fwd_fp8kv(const void* q, const void* kv_rows, int Nkv, const void* kv2_rows, int Nkv2, int n_nope,
+                             const float* attn_sink, const int32_t* topk_idxs, int B, int S, int H, int D, int K,
+                             int Dv, float softmax_scale, void* o, float* lse, void* ws, size_t ws_bytes,
+                             cudaStream_t stream) {
+  if (n_nope <= 0) return si::fail("sparse_attn_fwd_fp8kv: n_nope must be > 0");
+  return si::run_sparse_attn(q, kv_rows, Nkv, kv2_rows, Nkv2, attn_sink, topk_idxs, nullptr, 0, 0, 0, B, S, H, D, K,
+                             Dv, softmax_scale, o, lse, ws, ws_bytes, stream, n_nope);
 }
 
 int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,

@@ -1,9 +1,9 @@
 """Generate golden fixtures by running the reference's own Python functions.
 
-Run in a container that has the reference checkout (read-only) at
-``$STREAMINDEX_REF`` (default ``/root/reference``)::
+Run where a checkout of the reference exists, naming it by argument or by
+``$STREAMINDEX_REF``::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path-to-reference-checkout>
 
 The shipped reference drops the empty call parentheses of some method calls
 (``q.dim != 4``, ``qk.relu_``, ``(x).exp``, ``c_a.dim != 3``).  Rather than
@@ -27,7 +27,6 @@ import sys
 
 import torch
 
-REF = os.environ.get("STREAMINDEX_REF", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -76,6 +75,9 @@ def _load(name, path):
 
 
 def main():
+    REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("STREAMINDEX_REF")
+    if not REF or not os.path.isdir(REF):
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set $STREAMINDEX_REF)")
     sys.path.insert(0, REF)
     from flash_sparse import reference as R  # noqa: E402
     from flash_sparse import csa as C  # noqa: E402
@@ -139,6 +141,17 @@ def main():
     bx = torch.randn((8, 24), generator=g3)
     comp8 = plain(R.reference_token_compressor(fx(cx), fx(zx), fx(bx), 8, overlap=False))
     out["compress_gated"] = dict(c=cx, z=zx, b=bx, m=8, out=comp8)
+
+    # 6. FP8 KV quant-dequant of the NoPE dims, block 64 (flash_sparse/utils/quantization.py:19-36)
+    Q = _load("ref_quant", os.path.join(REF, "flash_sparse", "utils", "quantization.py"))
+    g4 = torch.Generator("cpu").manual_seed(23)
+    kvq = torch.randn((2, 24, 576), generator=g4)
+    kvq[0, :4] *= 40.0            # large rows
+    kvq[1, :3, :64] *= 1e-6       # a block below the 1e-4 amax floor
+    kvq[1, 5] = 0.0               # an all-zero row
+    kvq = kvq.bfloat16()
+    deq = plain(Q.act_quant_simulate(fx(kvq[..., :512].contiguous()), block_size=64))
+    out["kv_fp8"] = dict(kv=kvq, n_nope=512, block=64, deq=deq)
 
     only = os.environ.get("GOLDEN_ONLY")
     for name, d in out.items():

@@ -149,3 +149,59 @@ def test_sparse_attn_autograd_wrapper():
     assert out.requires_grad
     with pytest.raises(NotImplementedError):
         out.float().sum().backward()
+
+
+@pytest.mark.parametrize("D,n_nope", [(576, 512), (512, 448)])
+def test_kv_fp8_quantiser_bit_exact(golden, D, n_nope):
+    """si_kv_quant_fp8 writes the oracle's FP8 rows byte for byte (e4m3 codes,
+    fp32 scales, bf16 rope dims, zero pads); at D=576 on the reference golden."""
+    from oracle.kv_fp8 import quantize_rows
+    from streamindex_b200.attention import quantize_kv_fp8
+
+    if D == 576:
+        kv = golden("kv_fp8")["kv"]
+    else:
+        g = torch.Generator().manual_seed(31)
+        kv = (torch.randn((3, 50, D), generator=g) * torch.logspace(-3, 2, 50).view(1, -1, 1)).bfloat16()
+    got = quantize_kv_fp8(kv.cuda(), n_nope).cpu()
+    assert torch.equal(got, quantize_rows(kv, n_nope))
+
+
+@pytest.mark.parametrize("D,n_nope,d_v", [(576, 512, 512), (576, 512, None), (512, 448, 448)])
+def test_sparse_attn_fp8_rows(D, n_nope, d_v):
+    """Attention over FP8 KV rows equals attention over the dequantised bf16 kv
+    (same tile contents: bit-identical to the bf16 kernel) and the oracle on the
+    dequantised kv (atol 2e-2); masked slots and an all-masked query included."""
+    from oracle.kv_fp8 import dequantize_rows
+    from streamindex_b200.attention import quantize_kv_fp8, sparse_attn_fwd, sparse_attn_fwd_fp8kv
+
+    q, kv, sink, idx = oracle.attn_inputs(1, 150, 64, D, 300, 96, ratio=1, seed=D + n_nope)
+    idx[:, :, 5::6] = -1
+    idx[0, 7] = -1
+    rows = quantize_kv_fp8(kv.cuda(), n_nope)
+    deq = dequantize_rows(rows.cpu(), D, n_nope)
+    dvk = d_v if d_v is not None else D
+    o8, l8 = sparse_attn_fwd_fp8kv(q.cuda(), rows, n_nope, sink.cuda(), idx.cuda(), d_v=dvk)
+    ob, lb = sparse_attn_fwd(q.cuda(), deq.cuda(), sink.cuda(), idx.cuda(), d_v=dvk)
+    torch.cuda.synchronize()
+    assert torch.equal(o8, ob) and torch.equal(l8, lb)
+    ro, rl = oracle.sparse_attn(q, deq, sink, idx, d_v=dvk)
+    assert (o8.float().cpu() - ro).abs().max().item() <= 2e-2
+    torch.testing.assert_close(l8.cpu(), rl, atol=1e-3, rtol=1e-4)
+
+
+def test_full_width_576_single_pass_matches_two_width_passes():
+    """The default full-width output (D_v = D = 576) runs as one pass (value
+    columns 512..575 accumulate beside S in tensor memory); it equals the
+    d_v=512 output on the first 512 columns and the oracle on all 576."""
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    q, kv, sink, idx = oracle.attn_inputs(2, 300, 64, 576, 700, 80, ratio=1, seed=57)
+    idx[:, :, 2::9] = -1
+    o, lse = sparse_attn_fwd(q.cuda(), kv.cuda(), sink.cuda(), idx.cuda())
+    o512, lse512 = sparse_attn_fwd(q.cuda(), kv.cuda(), sink.cuda(), idx.cuda(), d_v=512)
+    torch.cuda.synchronize()
+    assert o.shape[-1] == 576
+    assert torch.equal(o[..., :512], o512) and torch.equal(lse, lse512)
+    ro, _ = oracle.sparse_attn(q, kv, sink, idx)
+    assert (o.float().cpu() - ro).abs().max().item() <= 2e-2

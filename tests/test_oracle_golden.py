@@ -111,3 +111,16 @@ def test_tie_certificate_accepts_ties_and_rejects_a_dropped_winner():
     except AssertionError:
         return
     raise AssertionError("a dropped winner passed the tie certificate")
+
+
+def test_kv_fp8_quant_matches_reference_simulation(golden):
+    """FP8 KV rows: the oracle's dequantised NoPE dims equal the reference's
+    act_quant_simulate(kv[..., :512], 64) bit for bit; rope dims pass through."""
+    from oracle.kv_fp8 import dequantize_rows, quantize_rows, row_layout
+
+    d = golden("kv_fp8")
+    rows = quantize_rows(d["kv"], d["n_nope"])
+    assert rows.shape[-1] == row_layout(576, 512)[1] == 672
+    deq = dequantize_rows(rows, 576, d["n_nope"])
+    assert torch.equal(deq[..., :512], d["deq"])
+    assert torch.equal(deq[..., 512:], d["kv"][..., 512:])
