@@ -178,6 +178,15 @@ SI_API int si_csa_sparse_attn_fwd(const void* q, const void* kv, int S_total, co
                                   long long s_offset, int B, int S, int H, int D, int Dv, float softmax_scale, void* o,
                                   float* lse, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+/* si_sparse_attn_fwd_kv2 with the element type of q / kv / o chosen by dtype:
+ * 0 = bf16, 1 = fp16 (the reference accepts either,
+ * flash_sparse/triton/sparse_attn_fwd.py:207).  In fp16 the probabilities P
+ * enter the P.V product as fp16 (both tensor-core operands share one type). */
+SI_API int si_sparse_attn_fwd_ex(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2,
+                                 const float* attn_sink, const int32_t* topk_idxs, int B, int S, int H, int D, int K,
+                                 int Dv, float softmax_scale, int dtype, void* o, float* lse, void* ws,
+                                 size_t ws_bytes, cudaStream_t stream);
+
 /* Top-k of a materialised score matrix [B,S,T] fp32 with the causal limit
  * t < (s+1)/causal_ratio (<= 0: none); same output contract as si_indexer_topk.
  * Replaces the masked_fill + topk + post-mask of build_csa_topk_idxs

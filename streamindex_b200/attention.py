@@ -4,6 +4,9 @@
 * :func:`sparse_attn`     — ``flash_sparse/triton/__init__.py:50-61`` (autograd
   wrapper; the backward pass is out of scope and raises ``NotImplementedError``)
 
+q / kv / o are bf16 or fp16 (one type for all three, as the reference's
+Triton kernel accepts, ``sparse_attn_fwd.py:207``).
+
 Semantics follow ``reference_sparse_attn`` (``flash_sparse/reference.py:44-130``):
 ``-1`` indices are masked, the sink enters the denominator only, the default
 scale is ``D**-0.5``, an all-masked query returns 0.  ``d_v`` (new keyword)
@@ -39,15 +42,16 @@ def _attn_call(q, kv, kv2, attn_sink, idx, softmax_scale, dv):
             kv2k = F.pad(kv2k, (0, Dp - D))
     idx = idx.to(device=dev, dtype=torch.int32).contiguous()
     sink = attn_sink.to(device=dev, dtype=torch.float32).contiguous()
-    o = torch.empty((B, S, H, dv_k), dtype=torch.bfloat16, device=dev)
+    o = torch.empty((B, S, H, dv_k), dtype=q.dtype, device=dev)
     lse = torch.empty((B, S, H), dtype=torch.float32, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
         ws = torch.empty(256, dtype=torch.uint8, device=dev)
-        _lib.check(lib.si_sparse_attn_fwd_kv2(
+        _lib.check(lib.si_sparse_attn_fwd_ex(
             qk.data_ptr(), kvk.data_ptr(), kvk.shape[1], _lib.ptr(kv2k), 0 if kv2k is None else kv2k.shape[1],
             sink.data_ptr(), idx.data_ptr() if K > 0 else None, B, S, H, Dp, K, dv_k, float(softmax_scale),
-            o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, _lib.stream_handle(dev)))
+            int(q.dtype == torch.float16), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256,
+            _lib.stream_handle(dev)))
         _lib.maybe_check_status(ws, dev, "sparse_attn_fwd")
     if dv_k != dv:
         o = o[..., :dv].contiguous()
@@ -98,8 +102,8 @@ def sparse_attn_fwd(
     del block_h, block_n  # Triton tiling knobs of the reference
     assert q.is_cuda and kv.is_cuda, "inputs must be CUDA tensors (no CPU fallback)"
     assert q.dim() == 4 and kv.dim() == 3
-    assert q.dtype == torch.bfloat16, f"q must be bf16, got {q.dtype}"
-    assert kv.dtype == q.dtype
+    assert q.dtype in (torch.bfloat16, torch.float16), f"q must be bf16 or fp16, got {q.dtype}"
+    assert kv.dtype == q.dtype, "q and kv must share one dtype"
     assert attn_sink.dtype == torch.float32
     B, S, H, D = q.shape
     B2, N_kv, D2 = kv.shape

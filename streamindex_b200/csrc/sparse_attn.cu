@@ -105,6 +105,7 @@ struct Params {
   // dequantised by the gather warps into the same bf16 stage layout:
   //   value = bf16(float(e4m3) * scale[block])
   int fp8, n_nope, row_bytes, rope_off;
+  int f16;             // q / kv / o are fp16 (else bf16); P is packed in the same type
   unsigned long long* trace;  // debug builds (SI_ATTN_TRACE) only: per-role timestamps of CTA 0
 };
 
@@ -350,10 +351,10 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
 #pragma unroll
         for (int kc = 0; kc < 2; ++kc) {
           uint4 u;
-          u.x = pack_bf16x2(sv[kc * 8 + 0], sv[kc * 8 + 1]);
-          u.y = pack_bf16x2(sv[kc * 8 + 2], sv[kc * 8 + 3]);
-          u.z = pack_bf16x2(sv[kc * 8 + 4], sv[kc * 8 + 5]);
-          u.w = pack_bf16x2(sv[kc * 8 + 6], sv[kc * 8 + 7]);
+          u.x = pack_x2(sv[kc * 8 + 0], sv[kc * 8 + 1], p.f16);
+          u.y = pack_x2(sv[kc * 8 + 2], sv[kc * 8 + 3], p.f16);
+          u.z = pack_x2(sv[kc * 8 + 4], sv[kc * 8 + 5], p.f16);
+          u.w = pack_x2(sv[kc * 8 + 6], sv[kc * 8 + 7], p.f16);
           *reinterpret_cast<uint4*>(prow + kc * 1024) = u;
         }
       }
@@ -394,7 +395,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       if (head < p.H) {
         uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j] * inv, v[2 * j + 1] * inv);
+        for (int j = 0; j < 16; ++j) w[j] = pack_x2(v[2 * j] * inv, v[2 * j + 1] * inv, p.f16);
         if (p.o_v8) {  // two 32-byte stores: half the store transactions of 16-byte ones
 #pragma unroll
           for (int j = 0; j < 16; j += 8)
@@ -782,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // are still in flight, and (a tcgen05.commit tracks only the issuing
     // thread's MMAs) an S completion never waits for a P.V.
     if (lane == 0) {
-      const uint32_t idesc1 = umma_idesc_f16(kHeads, NK, 1);
+      const uint32_t idesc1 = umma_idesc_f16(kHeads, NK, p.f16 ? 0 : 1);
       uint32_t st = 0, kph = 0;
       uint32_t sfr[2] = {0, 0};
       bool ok = true;
@@ -831,8 +832,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Tile j's kv stage is released here: its Q.K^T completed before the
     // softmax published P, so this commit covers every read of the stage.
     if (lane == 0) {
-      const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, 1) | (1u << 16);  // B (V) MN-major
-      const uint32_t idesc2x = umma_idesc_f16(kHeads, XV ? XV : 64, 1) | (1u << 16);
+      const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, p.f16 ? 0 : 1) | (1u << 16);  // B (V) MN-major
+      const uint32_t idesc2x = umma_idesc_f16(kHeads, XV ? XV : 64, p.f16 ? 0 : 1) | (1u << 16);
       uint32_t st = 0, pf[2] = {0, 0}, ofr = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
@@ -948,7 +949,7 @@ static inline Fp8RowLayout fp8_row_layout(int D, int n_nope) {
 static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
                            const int32_t* topk_idxs, const int64_t* comp, int comp_k, int nwin, long long s_off,
                            int B, int S, int H, int D, int K, int Dv, float softmax_scale, void* o, float* lse,
-                           void* ws, size_t ws_bytes, cudaStream_t stream, int fp8_n_nope = 0) {
+                           void* ws, size_t ws_bytes, cudaStream_t stream, int fp8_n_nope = 0, int f16 = 0) {
   if (Nkv2 < 0 || (Nkv2 > 0 && !kv2)) return fail("sparse_attn_fwd: bad second kv tensor");
   if (Nkv2 > 0 && (((uintptr_t)kv2) & 15)) return fail("sparse_attn_fwd: 16-byte alignment of kv2");
   const int Nkv1 = Nkv;
@@ -976,7 +977,8 @@ static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* k
   if (Nkv == 0) K = 0;
 
   CUtensorMap mq, mkv;
-  if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, attn::kHeads, 0)) return rc;
+  if (f16 && fp8_n_nope) return fail("sparse_attn_fwd: FP8 KV rows dequantise to bf16; q must be bf16");
+  if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, attn::kHeads, f16 ? 1 : 0)) return rc;
   if (fp8_n_nope) {
     if (fp8_n_nope % 64 || fp8_n_nope > 512 || D - fp8_n_nope <= 0 || D - fp8_n_nope > 64 || D % 8)
       return fail("sparse_attn_fwd_fp8kv: need n_nope a multiple of 64 in [64,512] and 0 < D - n_nope <= 64, "
@@ -986,7 +988,8 @@ static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* k
   // which are off for FP8 rows) then points at q like the empty-kv case.
   const void* kv_map_base = fp8_n_nope ? q : (Nkv1 > 0 ? kv : (Nkv2 > 0 ? kv2 : q));
   if (int rc = make_tmap_2d_16b(&mkv, kv_map_base, D,
-                                (uint64_t)(fp8_n_nope ? 1 : B * (Nkv1 > 0 ? Nkv1 : (Nkv2 > 0 ? Nkv2 : 1))), 64, 1, 0))
+                                (uint64_t)(fp8_n_nope ? 1 : B * (Nkv1 > 0 ? Nkv1 : (Nkv2 > 0 ? Nkv2 : 1))), 64, 1,
+                                f16 ? 1 : 0))
     return rc;
 
   attn::Params p{};
@@ -994,6 +997,7 @@ static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* k
   p.o_ld = Dv;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.idx = topk_idxs;
+  p.f16 = f16;
   p.comp = K > 0 ? reinterpret_cast<const long long*>(comp) : nullptr;
   p.comp_k = comp_k;
   p.nwin = nwin;
@@ -1085,6 +1089,14 @@ int si_sparse_attn_fwd_fp8kv(const void* q, const void* kv_rows, int Nkv, const 
   if (n_nope <= 0) return si::fail("sparse_attn_fwd_fp8kv: n_nope must be > 0");
   return si::run_sparse_attn(q, kv_rows, Nkv, kv2_rows, Nkv2, attn_sink, topk_idxs, nullptr, 0, 0, 0, B, S, H, D, K,
                              Dv, softmax_scale, o, lse, ws, ws_bytes, stream, n_nope);
+}
+
+int si_sparse_attn_fwd_ex(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
+                          const int32_t* topk_idxs, int B, int S, int H, int D, int K, int Dv, float softmax_scale,
+                          int dtype, void* o, float* lse, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (dtype != 0 && dtype != 1) return si::fail("sparse_attn_fwd: dtype must be 0 (bf16) or 1 (fp16), got %d", dtype);
+  return si::run_sparse_attn(q, kv, Nkv, kv2, Nkv2, attn_sink, topk_idxs, nullptr, 0, 0, 0, B, S, H, D, K, Dv,
+                             softmax_scale, o, lse, ws, ws_bytes, stream, 0, dtype);
 }
 
 int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,

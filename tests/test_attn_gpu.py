@@ -205,3 +205,20 @@ def test_full_width_576_single_pass_matches_two_width_passes():
     assert torch.equal(o[..., :512], o512) and torch.equal(lse, lse512)
     ro, _ = oracle.sparse_attn(q, kv, sink, idx)
     assert (o.float().cpu() - ro).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("D,d_v", [(576, 512), (128, None)])
+def test_fp16_inputs(D, d_v):
+    """fp16 q / kv (sparse_attn_fwd.py:207 accepts bf16 or fp16): fp16 output,
+    oracle parity at atol 2e-2 on the same fp16 inputs."""
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    q, kv, sink, idx = oracle.attn_inputs(2, 60, 64, D, 200, 48, ratio=1, seed=D + 3)
+    q16, kv16 = q.float().half(), kv.float().half()
+    idx[:, :, 4::5] = -1
+    o, lse = sparse_attn_fwd(q16.cuda(), kv16.cuda(), sink.cuda(), idx.cuda(), d_v=d_v)
+    torch.cuda.synchronize()
+    assert o.dtype == torch.float16
+    ro, rl = oracle.sparse_attn(q16, kv16, sink, idx, d_v=d_v)
+    assert (o.float().cpu() - ro).abs().max().item() <= 2e-2
+    torch.testing.assert_close(lse.cpu(), rl, atol=1e-3, rtol=1e-4)
