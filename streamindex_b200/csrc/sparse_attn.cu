@@ -61,6 +61,10 @@ constexpr int kQSlots = (512 - kQCol) / 32;  // 32-column Q atom slots in TMEM (
 // a Q ring shortened to kQSlotsXV slots, so D <= 768 there).
 constexpr int kXV = 64;
 constexpr int kQSlotsXV = (512 - kQCol - kXV) / 32;  // 12
+// Element modes (compile-time, so the bf16 path carries no per-element
+// branches): q / kv / o bf16, all fp16, or bf16 q / o over FP8 KV rows.
+enum AttnMode : int { kBf16 = 0, kF16 = 1, kFp8Rows = 2 };
+
 template <int XV>
 struct QRing {
   static constexpr int kSlots = XV ? kQSlotsXV : kQSlots;
@@ -200,7 +204,7 @@ __device__ __forceinline__ uint32_t stage_off(int a, int r, int ch) {
   return (uint32_t)(a * NK * 128 + r * 128) + ((uint32_t)(ch ^ (r & 7)) << 4);
 }
 
-template <int NK, int DVH, int XV>
+template <int NK, int DVH, int XV, int MODE>
 __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t* sP, uint32_t tmem, int warp,
                                              uint32_t lane, int nitems, int ntiles) {
   constexpr float kLn2 = 0.6931471805599453f;
@@ -351,10 +355,10 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
 #pragma unroll
         for (int kc = 0; kc < 2; ++kc) {
           uint4 u;
-          u.x = pack_x2(sv[kc * 8 + 0], sv[kc * 8 + 1], p.f16);
-          u.y = pack_x2(sv[kc * 8 + 2], sv[kc * 8 + 3], p.f16);
-          u.z = pack_x2(sv[kc * 8 + 4], sv[kc * 8 + 5], p.f16);
-          u.w = pack_x2(sv[kc * 8 + 6], sv[kc * 8 + 7], p.f16);
+          u.x = pack_x2(sv[kc * 8 + 0], sv[kc * 8 + 1], MODE == kF16);
+          u.y = pack_x2(sv[kc * 8 + 2], sv[kc * 8 + 3], MODE == kF16);
+          u.z = pack_x2(sv[kc * 8 + 4], sv[kc * 8 + 5], MODE == kF16);
+          u.w = pack_x2(sv[kc * 8 + 6], sv[kc * 8 + 7], MODE == kF16);
           *reinterpret_cast<uint4*>(prow + kc * 1024) = u;
         }
       }
@@ -395,7 +399,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
       if (head < p.H) {
         uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) w[j] = pack_x2(v[2 * j] * inv, v[2 * j + 1] * inv, p.f16);
+        for (int j = 0; j < 16; ++j) w[j] = pack_x2(v[2 * j] * inv, v[2 * j + 1] * inv, MODE == kF16);
         if (p.o_v8) {  // two 32-byte stores: half the store transactions of 16-byte ones
 #pragma unroll
           for (int j = 0; j < 16; j += 8)
@@ -416,7 +420,7 @@ __device__ __forceinline__ void attn_softmax(const Params& p, Misc* ms, uint8_t*
   }
 }
 
-template <int NK, int DVH, int XV>
+template <int NK, int DVH, int XV, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_kv,
                            Params p) {
@@ -718,7 +722,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         SI_TRACE_IF(tr, 0, ii, t, 1);
-        if (p.fp8) {
+        if (MODE == kFp8Rows) {
           // FP8 rows: this thread loads 16-byte chunks q = c + 8i of the row's
           // e4m3 part (64-dim block q/4 = atom q/4), the row's block scales and
           // rope chunk c, then writes the dequantised bf16 chunks into the stage.
@@ -783,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // are still in flight, and (a tcgen05.commit tracks only the issuing
     // thread's MMAs) an S completion never waits for a P.V.
     if (lane == 0) {
-      const uint32_t idesc1 = umma_idesc_f16(kHeads, NK, p.f16 ? 0 : 1);
+      const uint32_t idesc1 = umma_idesc_f16(kHeads, NK, MODE == kF16 ? 0 : 1);
       uint32_t st = 0, kph = 0;
       uint32_t sfr[2] = {0, 0};
       bool ok = true;
@@ -832,8 +836,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Tile j's kv stage is released here: its Q.K^T completed before the
     // softmax published P, so this commit covers every read of the stage.
     if (lane == 0) {
-      const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, p.f16 ? 0 : 1) | (1u << 16);  // B (V) MN-major
-      const uint32_t idesc2x = umma_idesc_f16(kHeads, XV ? XV : 64, p.f16 ? 0 : 1) | (1u << 16);
+      const uint32_t idesc2 = umma_idesc_f16(kHeads, NMMA, MODE == kF16 ? 0 : 1) | (1u << 16);  // B (V) MN-major
+      const uint32_t idesc2x = umma_idesc_f16(kHeads, XV ? XV : 64, MODE == kF16 ? 0 : 1) | (1u << 16);
       uint32_t st = 0, pf[2] = {0, 0}, ofr = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
@@ -878,7 +882,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    attn_softmax<NK, DVH, XV>(p, ms, sP, tmem, warp, lane, nitems, ntiles);
+    attn_softmax<NK, DVH, XV, MODE>(p, ms, sP, tmem, warp, lane, nitems, ntiles);
   }
 
   tc_fence_before();
@@ -897,28 +901,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 namespace si {
 namespace attn {
 
-template <int DVH, int XV = 0>
+template <int DVH, int XV, int MODE>
 static cudaError_t launch_t(const CUtensorMap& mq, const CUtensorMap& mkv, const Params& p, int grid,
                             cudaStream_t stream) {
   constexpr int NK = 32;
   static unsigned long long configured = 0;  // devices on which the attribute is set
-  cudaError_t e = set_smem_attr_once(reinterpret_cast<const void*>(sparse_attn_fwd_kernel<NK, DVH, XV>), kSmemMax,
+  cudaError_t e = set_smem_attr_once(reinterpret_cast<const void*>(sparse_attn_fwd_kernel<NK, DVH, XV, MODE>), kSmemMax,
                                      &configured);
   if (e != cudaSuccess) return e;
-  sparse_attn_fwd_kernel<NK, DVH, XV><<<grid, kThreads, smem_bytes<NK>(p.NA), stream>>>(mq, mkv, p);
+  sparse_attn_fwd_kernel<NK, DVH, XV, MODE><<<grid, kThreads, smem_bytes<NK>(p.NA), stream>>>(mq, mkv, p);
   return cudaGetLastError();
+}
+
+template <int MODE>
+static cudaError_t launch_m(const CUtensorMap& mq, const CUtensorMap& mkv, const Params& p, int grid,
+                            cudaStream_t stream) {
+  switch (p.Dv) {
+    case 64: return launch_t<32, 0, MODE>(mq, mkv, p, grid, stream);
+    case 128: return launch_t<64, 0, MODE>(mq, mkv, p, grid, stream);
+    case 256: return launch_t<128, 0, MODE>(mq, mkv, p, grid, stream);
+    case 512: return launch_t<256, 0, MODE>(mq, mkv, p, grid, stream);
+    case 512 + kXV: return launch_t<256, kXV, MODE>(mq, mkv, p, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 static cudaError_t launch(const CUtensorMap& mq, const CUtensorMap& mkv, const Params& p, int grid,
                           cudaStream_t stream) {
-  switch (p.Dv) {
-    case 64: return launch_t<32>(mq, mkv, p, grid, stream);
-    case 128: return launch_t<64>(mq, mkv, p, grid, stream);
-    case 256: return launch_t<128>(mq, mkv, p, grid, stream);
-    case 512: return launch_t<256>(mq, mkv, p, grid, stream);
-    case 512 + kXV: return launch_t<256, kXV>(mq, mkv, p, grid, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  if (p.fp8) return launch_m<kFp8Rows>(mq, mkv, p, grid, stream);
+  if (p.f16) return launch_m<kF16>(mq, mkv, p, grid, stream);
+  return launch_m<kBf16>(mq, mkv, p, grid, stream);
 }
 
 }  // namespace attn
