@@ -187,6 +187,20 @@ SI_API int si_sparse_attn_fwd_ex(const void* q, const void* kv, int Nkv, const v
                                  int Dv, float softmax_scale, int dtype, void* o, float* lse, void* ws,
                                  size_t ws_bytes, cudaStream_t stream);
 
+/* Sparse MQA attention backward with attention sink.
+ * Replaces sparse_attn_bwd (flash_sparse/triton/sparse_attn_bwd.py:286-416):
+ *   inputs as si_sparse_attn_fwd plus o [B,S,H,Dv] bf16 and lse [B,S,H] fp32
+ *   from the forward and dout [B,S,H,Dv] bf16;
+ *   dq      [B,S,H,D]  bf16   (written; zero it first when K == 0)
+ *   dkv_f32 [B,Nkv,D]  fp32   accumulated with atomic adds: zero it first
+ *   dsink   [H]        fp32   accumulated with atomic adds: zero it first
+ * D in {64,128,256,512,576}; Dv a multiple of 32, <= D (value = first Dv dims).
+ * bf16 only. */
+SI_API int si_sparse_attn_bwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs,
+                              const void* o, const float* lse, const void* dout, int B, int S, int H, int D, int Nkv,
+                              int K, int Dv, float softmax_scale, void* dq, float* dkv_f32, float* dsink,
+                              cudaStream_t stream);
+
 /* Top-k of a materialised score matrix [B,S,T] fp32 with the causal limit
  * t < (s+1)/causal_ratio (<= 0: none); same output contract as si_indexer_topk.
  * Replaces the masked_fill + topk + post-mask of build_csa_topk_idxs

@@ -22,7 +22,7 @@ from .indexer import (  # noqa: F401
     chunked_indexer_topk,
     topk_desc_stable,
 )
-from .attention import sparse_attn  # noqa: F401
+from .attention import sparse_attn, sparse_attn_grads  # noqa: F401
 from .csa import (  # noqa: F401
     sliding_window_idxs,
     build_csa_topk_idxs,

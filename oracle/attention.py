@@ -65,3 +65,14 @@ def sparse_attn(
         mm = m.squeeze(-1)
         lse[:, s0:s1] = torch.where(denom > 0, torch.log(denom) + mm, torch.full_like(denom, -1.0e30))
     return o, lse
+
+
+def sparse_attn_grads(q, kv, attn_sink, topk_idxs, do, softmax_scale=None, d_v=None):
+    """``(dq, dkv, dsink)`` of ``sum(sparse_attn(...)[0] * do)`` by autograd through :func:`sparse_attn`
+    in fp32 (the reference's backward math, ``flash_sparse/triton/sparse_attn_bwd.py:1-30``)."""
+    qf = q.detach().float().requires_grad_(True)
+    kvf = kv.detach().float().requires_grad_(True)
+    sf = attn_sink.detach().float().clone().requires_grad_(True)
+    o, _ = sparse_attn(qf, kvf, sf, topk_idxs, softmax_scale, d_v=d_v)
+    (o * do.float()).sum().backward()
+    return qf.grad, kvf.grad, sf.grad

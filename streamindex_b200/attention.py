@@ -1,8 +1,9 @@
 """Sparse MQA attention forward with attention sink, over the C ABI.
 
 * :func:`sparse_attn_fwd` — ``flash_sparse/triton/sparse_attn_fwd.py:180-292``
+* :func:`sparse_attn_bwd` — ``flash_sparse/triton/sparse_attn_bwd.py:286-416``
 * :func:`sparse_attn`     — ``flash_sparse/triton/__init__.py:50-61`` (autograd
-  wrapper; the backward pass is out of scope and raises ``NotImplementedError``)
+  wrapper over the two)
 
 q / kv / o are bf16 or fp16 (one type for all three, as the reference's
 Triton kernel accepts, ``sparse_attn_fwd.py:207``).
@@ -179,17 +180,64 @@ def sparse_attn_fwd_fp8kv(q: torch.Tensor, kv_rows: torch.Tensor, n_nope: int, a
     return o, lse
 
 
+def sparse_attn_bwd(q, kv, attn_sink, topk_idxs, o, lse, do, softmax_scale: Optional[float] = None, *,
+                    block_h: Optional[int] = None):
+    """Backward of :func:`sparse_attn_fwd` (``flash_sparse/triton/sparse_attn_bwd.py:286-416``).
+
+    ``o`` / ``lse`` are the forward's outputs and ``do`` the gradient of ``o``
+    (width ``d_v = o.shape[-1]``; the value is the first ``d_v`` dims of kv).
+    Returns ``(dq, dkv, dattn_sink)`` in the dtypes of ``q``, ``kv`` and
+    ``attn_sink``.  ``block_h`` is the reference's Triton tiling knob, ignored.
+    """
+    del block_h
+    assert q.is_cuda and kv.is_cuda and do.is_cuda
+    assert q.dtype == kv.dtype == do.dtype == torch.bfloat16, "backward supports bf16 tensors"
+    assert attn_sink.dtype == torch.float32 and lse.dtype == torch.float32
+    B, S, H, D = q.shape
+    N_kv = kv.shape[1]
+    K = topk_idxs.shape[-1]
+    Dv = o.shape[-1]
+    assert do.shape == o.shape == (B, S, H, Dv), "do must match o"
+    if D not in (64, 128, 256, 512, 576):
+        raise ValueError(f"backward supports D in (64, 128, 256, 512, 576), got {D}")
+    if Dv % 32 or Dv > D:
+        raise ValueError(f"backward needs d_v a multiple of 32 and <= D, got {Dv}")
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    dev = q.device
+    qk, kvk, ok, dok = q.contiguous(), kv.contiguous(), o.contiguous(), do.contiguous()
+    idx = topk_idxs.to(device=dev, dtype=torch.int32).contiguous()
+    sink = attn_sink.contiguous()
+    dq = torch.zeros_like(qk)
+    dkv = torch.zeros((B, N_kv, D), dtype=torch.float32, device=dev)
+    dsink = torch.zeros_like(sink)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().si_sparse_attn_bwd(
+            qk.data_ptr(), kvk.data_ptr(), sink.data_ptr(), idx.data_ptr() if K > 0 else None, ok.data_ptr(),
+            lse.contiguous().data_ptr(), dok.data_ptr(), B, S, H, D, N_kv, K, Dv, float(softmax_scale),
+            dq.data_ptr(), dkv.data_ptr(), dsink.data_ptr(), _lib.stream_handle(dev)))
+    return dq, dkv.to(kv.dtype), dsink
+
+
 class _SparseAttnFunc(torch.autograd.Function):
+    """Saves q, kv, attn_sink, topk_idxs, o and lse for the backward pass
+    (``flash_sparse/triton/__init__.py:19-47``)."""
+
     @staticmethod
     def forward(ctx, q, kv, attn_sink, topk_idxs, softmax_scale, d_v):
-        o, _ = sparse_attn_fwd(q, kv, attn_sink, topk_idxs, softmax_scale, d_v=d_v)
+        o, lse = sparse_attn_fwd(q, kv, attn_sink, topk_idxs, softmax_scale, d_v=d_v)
+        ctx.save_for_backward(q, kv, attn_sink, topk_idxs, o, lse)
+        ctx.softmax_scale = softmax_scale
         return o
 
     @staticmethod
     def backward(ctx, do):
-        raise NotImplementedError("sparse attention backward is not part of this build (forward only)")
+        q, kv, attn_sink, topk_idxs, o, lse = ctx.saved_tensors
+        dq, dkv, dsink = sparse_attn_bwd(q, kv, attn_sink, topk_idxs, o, lse, do.contiguous(), ctx.softmax_scale)
+        return dq, dkv, dsink, None, None, None
 
 
 def sparse_attn(q, kv, attn_sink, topk_idxs, softmax_scale: Optional[float] = None, *, d_v: Optional[int] = None):
-    """Forward of the reference's differentiable ``sparse_attn``; returns ``o`` only."""
+    """Differentiable sparse attention (``flash_sparse/triton/__init__.py:50-61``): forward
+    :func:`sparse_attn_fwd`, backward :func:`sparse_attn_bwd`.  Returns ``o`` only."""
     return _SparseAttnFunc.apply(q, kv, attn_sink, topk_idxs, softmax_scale, d_v)

@@ -153,6 +153,25 @@ def main():
     deq = plain(Q.act_quant_simulate(fx(kvq[..., :512].contiguous()), block_size=64))
     out["kv_fp8"] = dict(kv=kvq, n_nope=512, block=64, deq=deq)
 
+    # 7. gradients of the reference's sparse attention (autograd through
+    #    reference_sparse_attn itself): the backward's ground truth
+    #    (the reference's Triton backward needs a GPU and a power-of-2 D)
+    for name, shp, dv, seed in [("attn_bwd_576", dict(B=1, S=12, H=16, D=576, N=48, K=32), 512, 29),
+                                ("attn_bwd_128", dict(B=2, S=10, H=20, D=128, N=40, K=24), 128, 31)]:
+        q, kv, sink, idx = attn_inputs(shp["B"], shp["S"], shp["H"], shp["D"], shp["N"], shp["K"], ratio=1, seed=seed)
+        idx[0, 0] = -1
+        idx[:, :, 5::7] = -1
+        gdo = torch.Generator("cpu").manual_seed(seed + 1)
+        do = torch.randn((shp["B"], shp["S"], shp["H"], dv), generator=gdo).bfloat16()
+        qf = q.float().requires_grad_(True)
+        kvf = kv.float().requires_grad_(True)
+        sf = sink.clone().requires_grad_(True)
+        o = R.reference_sparse_attn(fx(qf), fx(kvf), fx(sf), fx(idx), softmax_scale=None)
+        o = plain(o)[..., :dv]
+        (o * do.float()).sum().backward()
+        out[name] = dict(q=q, kv=kv, sink=sink, idx=idx, do=do, d_v=dv, o=o.detach().float(),
+                         dq=qf.grad.detach(), dkv=kvf.grad.detach(), dsink=sf.grad.detach())
+
     only = os.environ.get("GOLDEN_ONLY")
     for name, d in out.items():
         if only and name not in only.split(","):

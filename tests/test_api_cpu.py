@@ -13,9 +13,13 @@ def test_flash_sparse_import_paths():
     from flash_sparse.triton import sparse_attn, sparse_attn_bwd, sparse_attn_fwd  # noqa: F401
     from flash_sparse.triton.chunked_indexer import chunked_indexer_topk  # noqa: F401
     from flash_sparse.triton.indexer_score import indexer_score, indexer_score_topk  # noqa: F401
+    from flash_sparse.triton.sparse_attn_bwd import sparse_attn_bwd as bwd2
 
-    with pytest.raises(NotImplementedError):
-        sparse_attn_bwd()
+    assert bwd2 is sparse_attn_bwd
+    z = torch.zeros(1, 2, 4, 64, dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):  # CPU tensors: no fallback
+        sparse_attn_bwd(z, torch.zeros(1, 3, 64, dtype=torch.bfloat16), torch.zeros(4),
+                        torch.zeros(1, 2, 2, dtype=torch.int32), z, torch.zeros(1, 2, 4), z)
 
 
 def test_no_cpu_fallback():

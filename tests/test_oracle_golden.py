@@ -124,3 +124,14 @@ def test_kv_fp8_quant_matches_reference_simulation(golden):
     deq = dequantize_rows(rows, 576, d["n_nope"])
     assert torch.equal(deq[..., :512], d["deq"])
     assert torch.equal(deq[..., 512:], d["kv"][..., 512:])
+
+
+def test_attention_grads_match_reference_autograd(golden):
+    """The oracle's backward (autograd through its sparse attention) equals the
+    gradients of the reference's own reference_sparse_attn."""
+    for name in ("attn_bwd_576", "attn_bwd_128"):
+        d = golden(name)
+        dq, dkv, ds = oracle.sparse_attn_grads(d["q"], d["kv"], d["sink"], d["idx"], d["do"], d_v=d["d_v"])
+        torch.testing.assert_close(dq, d["dq"], atol=1e-4, rtol=1e-4)
+        torch.testing.assert_close(dkv, d["dkv"], atol=1e-4, rtol=1e-4)
+        torch.testing.assert_close(ds, d["dsink"], atol=1e-4, rtol=1e-4)
