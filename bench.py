@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--attn-dv", type=int, default=512, help="attention workload: value width (576 = full D)")
     ap.add_argument("--kv-fp8", action="store_true",
                     help="attention workload: kv stored as FP8 rows (e4m3 NoPE + fp32 block scales + bf16 RoPE)")
-    ap.add_argument("--workload", default="indexer", choices=["indexer", "attn", "csa"],
+    ap.add_argument("--workload", default="indexer", choices=["indexer", "attn", "attn_bwd", "csa"],
                     help="indexer: the headline metric (default); attn: benchmark configs[3] sparse attention")
     return ap.parse_args()
 
@@ -520,6 +520,63 @@ def run_attn(a):
     print(json.dumps(line), flush=True)
 
 
+def run_attn_bwd(a):
+    """Sparse attention backward at the benchmark config-4 shape (B=1, S=65536, H=64, D=576/512,
+    N_kv=16384, K=512): one step = si_sparse_attn_bwd (dq, dkv, dsink) given the forward's o / lse."""
+    from streamindex_b200 import _lib
+    from streamindex_b200.attention import sparse_attn_fwd
+
+    S, H, D, DV, NKV, K = a.S, a.attn_heads, 576, a.attn_dv, 16384, a.attn_k
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    q = torch.randn((1, S, H, D), generator=g, device=device, dtype=torch.bfloat16).mul_(D ** -0.5)
+    kv = torch.randn((1, NKV, D), generator=g, device=device, dtype=torch.bfloat16)
+    sink = torch.zeros(H, dtype=torch.float32, device=device)
+    idx = gen_attn_idx(S, K, NKV, 4, device)
+    o, lse = sparse_attn_fwd(q, kv, sink, idx, d_v=DV)
+    do = torch.randn(o.shape, generator=g, device=device, dtype=torch.bfloat16)
+    dq = torch.zeros_like(q)
+    dkv = torch.zeros((1, NKV, D), dtype=torch.float32, device=device)
+    dsink = torch.zeros(H, dtype=torch.float32, device=device)
+    lib = _lib.load()
+    st = _lib.stream_handle(device)
+
+    def step():
+        dkv.zero_()
+        dsink.zero_()
+        _lib.check(lib.si_sparse_attn_bwd(q.data_ptr(), kv.data_ptr(), sink.data_ptr(), idx.data_ptr(), o.data_ptr(),
+                                          lse.data_ptr(), do.data_ptr(), 1, S, H, D, NKV, K, DV, D ** -0.5,
+                                          dq.data_ptr(), dkv.data_ptr(), dsink.data_ptr(), st))
+
+    for _ in range(a.warmup):
+        step()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / a.steps
+    V = int((idx >= 0).sum().item())
+    flops = 2.0 * H * V * (3 * D + 2 * DV)  # S, dO.V^T, dq, dkv (q and do parts)
+    peaks = _load_peaks()
+    tf_peak = peaks.get("bf16_tflops", 1590.0)
+    tf = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "sparse attention backward (benchmark configs[3] shape) Mqueries/s", "value": S / (ms * 1e-3) / 1e6,
+        "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"sparse_attn_bwd B=1 S={S} H={H} D=576 D_v={DV} N_kv=16384 K={K}",
+                   "valid_slots": V},
+        "gpu_launches": 3 * a.steps,
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": tf_peak, "unit": "TFLOP/s", "frac": tf / tf_peak,
+                     "peak_source": "of measured (bf16_tflops burst, tcgen05 cuBLAS); this kernel uses the "
+                                    "warp-level mma.sync path", "traffic": None},
+    }), flush=True)
+
+
 def _csa_slots(S, lo, hi, nwin, k, m):
     """Valid attention slots of queries [lo, hi): window min(n_win, s+1) + compressed min(k, (s+1)//m)."""
     import numpy as np
@@ -790,10 +847,10 @@ def main():
             dist.barrier()
             dist.destroy_process_group()
         return
-    if a.workload == "attn":
+    if a.workload in ("attn", "attn_bwd"):
         if a.S == 1 << 20:
             a.S = 65536
-        run_attn(a)
+        run_attn(a) if a.workload == "attn" else run_attn_bwd(a)
         return
     if a.impl == "reference":
         # CPU-only arm: rank 0 alone measures on the host cores; other ranks exit
