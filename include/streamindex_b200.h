@@ -74,6 +74,20 @@ SI_API int si_indexer_topk_ex(const void* q, const void* k, const void* w, int w
                               long long s_offset, unsigned flags, int64_t* out_idx, float* out_scores, void* ws,
                               size_t ws_bytes, cudaStream_t stream);
 
+/* si_indexer_topk_ex over strided inputs (the reference passes arbitrary
+ * strides to its kernels, flash_sparse/triton/indexer_score.py:162-170; here
+ * the last dimension must be contiguous):
+ *   q_strides {b, s, h} and k_strides {b, t}: element strides, multiples of 8;
+ *   w_strides {b, s, h}: element strides of w;
+ *   a null stride array means that tensor is contiguous.
+ * q and k are read in place through 4-D / 3-D tensor maps (no copy). */
+SI_API int si_indexer_topk_strided(const void* q, const long long* q_strides, const void* k,
+                                   const long long* k_strides, const void* w, const long long* w_strides,
+                                   int w_is_bf16, int ab_fp16, int B, int S, int T, int H, int D, int top_k,
+                                   int causal_ratio, const uint8_t* causal_mask, long long s_offset, unsigned flags,
+                                   int64_t* out_idx, float* out_scores, void* ws, size_t ws_bytes,
+                                   cudaStream_t stream);
+
 /* Sorts `rows` rows of top_k selection keys (as left by SI_FLAG_SKIP_SORT)
  * descending and decodes them in place into int64 indices (-1 pads) and
  * fp32 scores (-inf pads). */
@@ -186,6 +200,15 @@ SI_API int si_sparse_attn_fwd_ex(const void* q, const void* kv, int Nkv, const v
                                  const float* attn_sink, const int32_t* topk_idxs, int B, int S, int H, int D, int K,
                                  int Dv, float softmax_scale, int dtype, void* o, float* lse, void* ws,
                                  size_t ws_bytes, cudaStream_t stream);
+
+/* si_sparse_attn_fwd_ex with a strided q (element strides {b, s, h}, multiples
+ * of 8, last dimension contiguous; null = contiguous), read in place through a
+ * 4-D tensor map (sparse_attn_fwd.py:267-270 of the reference passes q's
+ * strides to its kernel).  kv, indices and outputs are contiguous. */
+SI_API int si_sparse_attn_fwd_strided(const void* q, const long long* q_strides, const void* kv, int Nkv,
+                                      const void* kv2, int Nkv2, const float* attn_sink, const int32_t* topk_idxs,
+                                      int B, int S, int H, int D, int K, int Dv, float softmax_scale, int dtype,
+                                      void* o, float* lse, void* ws, size_t ws_bytes, cudaStream_t stream);
 
 /* Sparse MQA attention backward with attention sink.
  * Replaces sparse_attn_bwd (flash_sparse/triton/sparse_attn_bwd.py:286-416):

@@ -29,6 +29,13 @@ SIGNATURES = {
     "si_indexer_topk_ex": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                    c_int, c_int, c_void_p, ctypes.c_longlong, ctypes.c_uint, c_void_p, c_void_p,
                                    c_void_p, c_size_t, c_void_p]),
+    "si_indexer_topk_strided": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                        c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                        ctypes.c_longlong, ctypes.c_uint, c_void_p, c_void_p, c_void_p, c_size_t,
+                                        c_void_p]),
+    "si_sparse_attn_fwd_strided": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                           c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p,
+                                           c_void_p, c_void_p, c_size_t, c_void_p]),
     "si_topk_row_sort": (c_int, [c_void_p, c_void_p, ctypes.c_longlong, c_int, c_void_p]),
     "si_indexer_topk_noalloc_max_ws_bytes": (c_size_t, []),
     "si_indexer_topk_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
@@ -104,6 +111,18 @@ def check(rc: int):
 
 def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+def strides_arg(t, dims, align_elems: int = 8):
+    """ctypes ``long long[len(dims)]`` of ``t``'s element strides over ``dims``
+    when ``t`` can be read in place (last dim contiguous, those strides
+    non-negative multiples of ``align_elems``, 16-byte aligned base), else None."""
+    if t.stride(-1) != 1 or t.data_ptr() % 16:
+        return None
+    st = [t.stride(d) for d in dims]
+    if any(x < 0 or x % align_elems for x in st):
+        return None
+    return (ctypes.c_longlong * len(st))(*st)
 
 
 def stream_handle(device) -> int:

@@ -34,7 +34,9 @@ def _attn_call(q, kv, kv2, attn_sink, idx, softmax_scale, dv):
     K = idx.shape[-1]
     dv_k = ((dv + 63) // 64) * 64
     Dp = ((max(D, dv_k) + 7) // 8) * 8
-    qk, kvk = q.contiguous(), kv.contiguous()
+    qs = _lib.strides_arg(q, (0, 1, 2)) if Dp == D else None
+    qk = q if qs is not None else q.contiguous()  # q is read in place when its last dim is contiguous
+    kvk = kv.contiguous()
     kv2k = None if kv2 is None else kv2.contiguous()
     if Dp != D:
         qk = F.pad(qk, (0, Dp - D))
@@ -48,8 +50,8 @@ def _attn_call(q, kv, kv2, attn_sink, idx, softmax_scale, dv):
     lib = _lib.load()
     with torch.cuda.device(dev):
         ws = torch.empty(256, dtype=torch.uint8, device=dev)
-        _lib.check(lib.si_sparse_attn_fwd_ex(
-            qk.data_ptr(), kvk.data_ptr(), kvk.shape[1], _lib.ptr(kv2k), 0 if kv2k is None else kv2k.shape[1],
+        _lib.check(lib.si_sparse_attn_fwd_strided(
+            qk.data_ptr(), qs, kvk.data_ptr(), kvk.shape[1], _lib.ptr(kv2k), 0 if kv2k is None else kv2k.shape[1],
             sink.data_ptr(), idx.data_ptr() if K > 0 else None, B, S, H, Dp, K, dv_k, float(softmax_scale),
             int(q.dtype == torch.float16), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256,
             _lib.stream_handle(dev)))

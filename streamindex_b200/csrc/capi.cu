@@ -63,6 +63,31 @@ int make_tmap_2d_16b(CUtensorMap* map, const void* base, int cols, uint64_t rows
   return 0;
 }
 
+int make_tmap_nd_16b(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* byte_strides, const uint32_t* box, int dtype) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail("cuTensorMapEncodeTiled is unavailable from the driver");
+  if (rank < 2 || rank > 5) return fail("tensor map: rank %d outside [2,5]", rank);
+  if (((uintptr_t)base) & 15) return fail("tensor map: base not 16-byte aligned");
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i] > 0 ? dims[i] : 1;
+    bx[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    if (byte_strides[i] % 16) return fail("tensor map: stride %d (%llu bytes) not a multiple of 16", i + 1,
+                                          (unsigned long long)byte_strides[i]);
+    st[i] = byte_strides[i];
+  }
+  CUresult r = fn(map, dtype ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank,
+                  const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled (rank %d) failed (CUresult %d)", rank, (int)r);
+  return 0;
+}
+
 cudaError_t set_smem_attr_once(const void* func, int bytes, unsigned long long* seen) {
   static std::mutex mu;
   int dev = 0;

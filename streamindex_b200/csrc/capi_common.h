@@ -19,6 +19,11 @@ int make_tmap_2d_16b(CUtensorMap* map, const void* base, int cols, uint64_t rows
                      int dtype);
 // Sets a kernel's max dynamic shared memory once per (kernel, device); thread safe.
 // `seen` is a per-kernel bitmask of devices already configured.
+// N-D (rank 2..5) tensor of 16-bit elements, dims[0] innermost and contiguous;
+// byte_strides[i] is the stride of dimension i+1 (multiples of 16 bytes), box
+// per dimension, the 128-byte swizzle.  dtype: 0 bf16, 1 fp16.
+int make_tmap_nd_16b(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* byte_strides, const uint32_t* box, int dtype);
 cudaError_t set_smem_attr_once(const void* func, int bytes, unsigned long long* seen);
 cudaError_t launch_fill_pad(int64_t* idx, float* scores, long long n, cudaStream_t stream);
 

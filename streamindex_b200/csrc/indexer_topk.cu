@@ -425,7 +425,7 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
       const int s = s0 + x / H;
       float wv = 0.f;
       if (s < p.S) {
-        const size_t off = ((size_t)b * p.S + s) * H + (x % H);
+        const long long off = b * p.w_sb + s * p.w_ss + (long long)(x % H) * p.w_sh;
         wv = p.w_is_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.w)[off])
                          : reinterpret_cast<const float*>(p.w)[off];
       }
@@ -641,12 +641,11 @@ __global__ void __launch_bounds__(EpiCfg<H>::THREADS, 1)
         if (!mbar_wait(&ms->q_empty, qph ^ 1, abort_flag, p.status, kErrWaitQ)) break;
         qph ^= 1;
         mbar_expect_tx(&ms->q_full, qbytes);
-        const int qrow = (b * p.S + blk * QC) * H;
+        // 256 (query, head) rows per box: 256/H queries x all H heads
         for (int a = 0; a < NA; ++a)
           for (int hh = 0; hh < 2; ++hh)
-            tma_load_2d(sQ + (size_t)a * kQRows * 128 + hh * 256 * 128, &map_q, &ms->q_full, a * 64,
-                        qrow + hh * 256);
-        const int krow = b * p.T;
+            tma_load_4d(sQ + (size_t)a * kQRows * 128 + hh * 256 * 128, &map_q, &ms->q_full, a * 64, 0,
+                        blk * QC + hh * (256 / H), b);
         bool ok = true;
         for (int t = 0; t < ntiles; ++t) {
           SI_ITRACE(0, r, t, 0);
@@ -658,8 +657,8 @@ __global__ void __launch_bounds__(EpiCfg<H>::THREADS, 1)
           mbar_expect_tx(&ms->k_full[st], kbytes);
           uint8_t* dst = sK + (size_t)st * NA * kKeysPerTile * 128;
           for (int a = 0; a < NA; ++a)
-            tma_load_2d(dst + (size_t)a * kKeysPerTile * 128, &map_k, &ms->k_full[st], a * 64,
-                        krow + t * kKeysPerTile);
+            tma_load_3d(dst + (size_t)a * kKeysPerTile * 128, &map_k, &ms->k_full[st], a * 64, t * kKeysPerTile,
+                        b);
           if (++st == (uint32_t)NST) {
             st = 0;
             kph ^= 1;
@@ -891,11 +890,20 @@ extern "C" SI_API void si_debug_set_sel_trace(unsigned long long* t) {
 namespace si {
 #endif
 
+// Element strides of the indexer inputs (last dim contiguous).  Negative
+// entries mean "contiguous" for that tensor.
+struct IndexerStrides {
+  long long q_b = -1, q_s = -1, q_h = -1, k_b = -1, k_t = -1, w_b = -1, w_s = -1, w_h = -1;
+};
+
 static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf16, int ab_fp16, int B, int S, int T,
                        int H, int D, int ksel, int ratio, const uint8_t* mask, int mode, int64_t* out_idx,
                        float* out_scores, void* ws, size_t ws_bytes, cudaStream_t stream, long long s_offset = 0,
-                       unsigned flags = 0) {
+                       unsigned flags = 0, IndexerStrides str = IndexerStrides()) {
   if (int rc = check_indexer_args(q, k, w, B, S, T, H, D)) return rc;
+  if (str.q_h < 0) { str.q_h = D; str.q_s = (long long)H * D; str.q_b = (long long)S * H * D; }
+  if (str.k_t < 0) { str.k_t = D; str.k_b = (long long)T * D; }
+  if (str.w_h < 0) { str.w_h = 1; str.w_s = H; str.w_b = (long long)S * H; }
   if (s_offset < 0) return fail("indexer: negative s_offset");
   if (!ws) return fail("indexer: null workspace");
   const size_t need = mode == kModeScore ? kStatusBytes : indexer_ws_bytes(B, S, H, ksel);
@@ -913,8 +921,16 @@ static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf1
   const int Dp = ((D + 63) / 64) * 64;
   CUtensorMap mq, mk;
   const int dt = ab_fp16 ? 1 : 0;
-  if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, 256, dt)) return rc;
-  if (int rc = make_tmap_2d_16b(&mk, k, D, (uint64_t)B * T, 64, kKeysPerTile, dt)) return rc;
+  {
+    const uint64_t qd[4] = {(uint64_t)D, (uint64_t)H, (uint64_t)S, (uint64_t)B};
+    const uint64_t qs[3] = {(uint64_t)str.q_h * 2, (uint64_t)str.q_s * 2, (uint64_t)str.q_b * 2};
+    const uint32_t qb[4] = {64, (uint32_t)H, (uint32_t)(256 / H), 1};
+    if (int rc = make_tmap_nd_16b(&mq, q, 4, qd, qs, qb, dt)) return rc;
+    const uint64_t kd[3] = {(uint64_t)D, (uint64_t)T, (uint64_t)B};
+    const uint64_t ks[2] = {(uint64_t)str.k_t * 2, (uint64_t)str.k_b * 2};
+    const uint32_t kb[3] = {64, (uint32_t)kKeysPerTile, 1};
+    if (int rc = make_tmap_nd_16b(&mk, k, 3, kd, ks, kb, dt)) return rc;
+  }
 
   IndexerParams p{};
   p.B = B; p.S = S; p.T = T; p.H = H; p.D = Dp;
@@ -931,6 +947,9 @@ static int run_indexer(const void* q, const void* k, const void* w, int w_is_bf1
   const int QC = kQRows / H;
   p.nblk_per_batch = ceil_div(S, QC);
   p.s_offset = s_offset;
+  p.w_sb = str.w_b;
+  p.w_ss = str.w_s;
+  p.w_sh = str.w_h;
 #ifdef SI_IDX_TRACE
   p.trace = g_idx_trace;
 #endif
@@ -980,6 +999,33 @@ int si_indexer_topk_ex(const void* q, const void* k, const void* w, int w_is_bf1
   const int mode = causal_ratio > 0 ? si::kModeTopk : (causal_mask ? si::kModeTopkMask : si::kModeTopk);
   return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, top_k, causal_ratio > 0 ? causal_ratio : 0,
                          causal_mask, mode, out_idx, out_scores, ws, ws_bytes, stream, s_offset, flags);
+}
+
+int si_indexer_topk_strided(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                            const void* w, const long long* w_strides, int w_is_bf16, int ab_fp16, int B, int S,
+                            int T, int H, int D, int top_k, int causal_ratio, const uint8_t* causal_mask,
+                            long long s_offset, unsigned flags, int64_t* out_idx, float* out_scores, void* ws,
+                            size_t ws_bytes, cudaStream_t stream) {
+  if (top_k < 1 || top_k > 2048) return si::fail("indexer_topk: top_k must be in [1, 2048] (got %d)", top_k);
+  if (!out_idx || !out_scores) return si::fail("indexer_topk: null output pointer");
+  si::IndexerStrides st;
+  if (q_strides) {
+    st.q_b = q_strides[0]; st.q_s = q_strides[1]; st.q_h = q_strides[2];
+    if (st.q_b < 0 || st.q_s < 0 || st.q_h < 0 || (st.q_b | st.q_s | st.q_h) % 8)
+      return si::fail("indexer_topk: q strides must be non-negative multiples of 8 elements");
+  }
+  if (k_strides) {
+    st.k_b = k_strides[0]; st.k_t = k_strides[1];
+    if (st.k_b < 0 || st.k_t < 0 || (st.k_b | st.k_t) % 8)
+      return si::fail("indexer_topk: k strides must be non-negative multiples of 8 elements");
+  }
+  if (w_strides) {
+    st.w_b = w_strides[0]; st.w_s = w_strides[1]; st.w_h = w_strides[2];
+    if (st.w_b < 0 || st.w_s < 0 || st.w_h < 0) return si::fail("indexer_topk: w strides must be non-negative");
+  }
+  const int mode = causal_ratio > 0 ? si::kModeTopk : (causal_mask ? si::kModeTopkMask : si::kModeTopk);
+  return si::run_indexer(q, k, w, w_is_bf16, ab_fp16, B, S, T, H, D, top_k, causal_ratio > 0 ? causal_ratio : 0,
+                         causal_mask, mode, out_idx, out_scores, ws, ws_bytes, stream, s_offset, flags, st);
 }
 
 int si_topk_row_sort(int64_t* idx_keys, float* out_scores, long long rows, int top_k, cudaStream_t stream) {

@@ -496,10 +496,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int bs = it / p.hgroups;
       const int nx = it + (int)gridDim.x;
       if (nx < nitems && lane < NA) {  // next item's Q into L2 while this one runs
-        const int nrow = (nx / p.hgroups) * p.H + (nx % p.hgroups) * kHeads;
-        tma_prefetch_l2_2d(&map_q, (int)lane * 64, nrow);
+        const int nbs = nx / p.hgroups;
+        tma_prefetch_l2_4d(&map_q, (int)lane * 64, (nx % p.hgroups) * kHeads, nbs % p.S, nbs / p.S);
       }
-      const int qrow = bs * p.H + hg * kHeads;
+      const int qs = bs % p.S, qb = bs / p.S;
       // Q atoms through the staging ring; the loader warps move them to TMEM
       bool ok = true;
       for (int a = 0; a < NA; ++a) {
@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) {
           mbar_expect_tx(&ms->qs_full[qslot], (uint32_t)kHeads * 128);
-          tma_load_2d(sQ + qslot * kHeads * 128, &map_q, &ms->qs_full[qslot], a * 64, qrow);
+          tma_load_4d(sQ + qslot * kHeads * 128, &map_q, &ms->qs_full[qslot], a * 64, hg * kHeads, qs, qb);
         }
         __syncwarp();
         if (++qslot == (uint32_t)kQStage) {
@@ -961,7 +961,8 @@ static inline Fp8RowLayout fp8_row_layout(int D, int n_nope) {
 static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* kv2, int Nkv2, const float* attn_sink,
                            const int32_t* topk_idxs, const int64_t* comp, int comp_k, int nwin, long long s_off,
                            int B, int S, int H, int D, int K, int Dv, float softmax_scale, void* o, float* lse,
-                           void* ws, size_t ws_bytes, cudaStream_t stream, int fp8_n_nope = 0, int f16 = 0) {
+                           void* ws, size_t ws_bytes, cudaStream_t stream, int fp8_n_nope = 0, int f16 = 0,
+                           const long long* q_strides = nullptr) {
   if (Nkv2 < 0 || (Nkv2 > 0 && !kv2)) return fail("sparse_attn_fwd: bad second kv tensor");
   if (Nkv2 > 0 && (((uintptr_t)kv2) & 15)) return fail("sparse_attn_fwd: 16-byte alignment of kv2");
   const int Nkv1 = Nkv;
@@ -990,7 +991,21 @@ static int run_sparse_attn(const void* q, const void* kv, int Nkv, const void* k
 
   CUtensorMap mq, mkv;
   if (f16 && fp8_n_nope) return fail("sparse_attn_fwd: FP8 KV rows dequantise to bf16; q must be bf16");
-  if (int rc = make_tmap_2d_16b(&mq, q, D, (uint64_t)B * S * H, 64, attn::kHeads, f16 ? 1 : 0)) return rc;
+  {
+    // q as a 4-D [B,S,H,D] map (element strides q_strides = {b, s, h}, or contiguous)
+    long long sb = (long long)S * H * D, ss = (long long)H * D, sh = D;
+    if (q_strides) {
+      sb = q_strides[0];
+      ss = q_strides[1];
+      sh = q_strides[2];
+      if (sb < 0 || ss < 0 || sh < 0 || (sb | ss | sh) % 8)
+        return fail("sparse_attn_fwd: q strides must be non-negative multiples of 8 elements");
+    }
+    const uint64_t qd[4] = {(uint64_t)D, (uint64_t)H, (uint64_t)S, (uint64_t)B};
+    const uint64_t qst[3] = {(uint64_t)sh * 2, (uint64_t)ss * 2, (uint64_t)sb * 2};
+    const uint32_t qbx[4] = {64, (uint32_t)attn::kHeads, 1, 1};
+    if (int rc = make_tmap_nd_16b(&mq, q, 4, qd, qst, qbx, f16 ? 1 : 0)) return rc;
+  }
   if (fp8_n_nope) {
     if (fp8_n_nope % 64 || fp8_n_nope > 512 || D - fp8_n_nope <= 0 || D - fp8_n_nope > 64 || D % 8)
       return fail("sparse_attn_fwd_fp8kv: need n_nope a multiple of 64 in [64,512] and 0 < D - n_nope <= 64, "
@@ -1109,6 +1124,15 @@ int si_sparse_attn_fwd_ex(const void* q, const void* kv, int Nkv, const void* kv
   if (dtype != 0 && dtype != 1) return si::fail("sparse_attn_fwd: dtype must be 0 (bf16) or 1 (fp16), got %d", dtype);
   return si::run_sparse_attn(q, kv, Nkv, kv2, Nkv2, attn_sink, topk_idxs, nullptr, 0, 0, 0, B, S, H, D, K, Dv,
                              softmax_scale, o, lse, ws, ws_bytes, stream, 0, dtype);
+}
+
+int si_sparse_attn_fwd_strided(const void* q, const long long* q_strides, const void* kv, int Nkv, const void* kv2,
+                               int Nkv2, const float* attn_sink, const int32_t* topk_idxs, int B, int S, int H, int D,
+                               int K, int Dv, float softmax_scale, int dtype, void* o, float* lse, void* ws,
+                               size_t ws_bytes, cudaStream_t stream) {
+  if (dtype != 0 && dtype != 1) return si::fail("sparse_attn_fwd: dtype must be 0 (bf16) or 1 (fp16), got %d", dtype);
+  return si::run_sparse_attn(q, kv, Nkv, kv2, Nkv2, attn_sink, topk_idxs, nullptr, 0, 0, 0, B, S, H, D, K, Dv,
+                             softmax_scale, o, lse, ws, ws_bytes, stream, 0, dtype, q_strides);
 }
 
 int si_sparse_attn_fwd(const void* q, const void* kv, const float* attn_sink, const int32_t* topk_idxs, int B, int S,

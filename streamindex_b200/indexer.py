@@ -29,7 +29,8 @@ from . import _lib
 _HEADS = (16, 32, 64, 128)
 
 
-def _prep(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor):
+def _check(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor):
+    """Shape / dtype / device checks shared by the wrappers (AssertionError / ValueError as the reference)."""
     assert q.is_cuda and k_idx.is_cuda and weights.is_cuda, "inputs must be CUDA tensors (no CPU fallback)"
     assert q.dim() == 4 and k_idx.dim() == 3 and weights.dim() == 3
     B, S, H, D = q.shape
@@ -42,6 +43,11 @@ def _prep(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor):
         raise ValueError(f"H_I ({H}) must be one of {_HEADS}")
     if D % 8 != 0 or D > 128:
         raise ValueError(f"D_I ({D}) must be a multiple of 8 and at most 128")
+    return B, S, H, D, T
+
+
+def _prep(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor):
+    B, S, H, D, T = _check(q, k_idx, weights)
     q = q.contiguous()
     k_idx = k_idx.contiguous()
     if weights.dtype not in (torch.float32, torch.bfloat16):
@@ -50,8 +56,25 @@ def _prep(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor):
     return q, k_idx, weights, (B, S, H, D, T)
 
 
+def _prep_strided(q: torch.Tensor, k_idx: torch.Tensor, weights: torch.Tensor):
+    """Like :func:`_prep`, but q / k_idx / weights whose last dim is contiguous
+    are passed in place with their strides (the reference hands its kernels
+    arbitrary strides); only other layouts are copied."""
+    B, S, H, D, T = _check(q, k_idx, weights)
+    qs = _lib.strides_arg(q, (0, 1, 2))
+    ks = _lib.strides_arg(k_idx, (0, 1))
+    if weights.dtype not in (torch.float32, torch.bfloat16):
+        weights = weights.float()
+    ws_ = _lib.strides_arg(weights, (0, 1, 2), align_elems=1) if weights.stride(-1) >= 0 else None
+    if ws_ is None or weights.data_ptr() % weights.element_size():
+        weights, ws_ = weights.contiguous(), None
+    q2 = q if qs is not None else q.contiguous()
+    k2 = k_idx if ks is not None else k_idx.contiguous()
+    return q2, qs, k2, ks, weights, ws_, (B, S, H, D, T)
+
+
 def _topk(q, k_idx, weights, top_k: int, width: int, ratio: Optional[int], mask: Optional[torch.Tensor]):
-    q, k_idx, weights, (B, S, H, D, T) = _prep(q, k_idx, weights)
+    q, qs, k_idx, ks, weights, ws_, (B, S, H, D, T) = _prep_strided(q, k_idx, weights)
     dev = q.device
     out_idx = torch.empty((B, S, width), dtype=torch.int64, device=dev)
     out_scores = torch.empty((B, S, width), dtype=torch.float32, device=dev)
@@ -62,9 +85,9 @@ def _topk(q, k_idx, weights, top_k: int, width: int, ratio: Optional[int], mask:
         m = None
         if mask is not None:
             m = mask.to(device=dev, dtype=torch.bool).expand(B, S, T).contiguous().view(torch.uint8)
-        _lib.check(lib.si_indexer_topk(
-            q.data_ptr(), k_idx.data_ptr(), weights.data_ptr(), int(weights.dtype == torch.bfloat16),
-            int(q.dtype == torch.float16), B, S, T, H, D, width, int(ratio or 0), _lib.ptr(m),
+        _lib.check(lib.si_indexer_topk_strided(
+            q.data_ptr(), qs, k_idx.data_ptr(), ks, weights.data_ptr(), ws_, int(weights.dtype == torch.bfloat16),
+            int(q.dtype == torch.float16), B, S, T, H, D, width, int(ratio or 0), _lib.ptr(m), 0, 0,
             out_idx.data_ptr(), out_scores.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_handle(dev)))
         _lib.maybe_check_status(ws, dev, "indexer_topk")
     return out_idx, out_scores
