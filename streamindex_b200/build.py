@@ -24,6 +24,9 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OUT_DIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(OUT_DIR, "libstreamindex_b200.so")
+# debug build of the same sources with the attention kernel's per-tile
+# %globaltimer stamps compiled in (SI_ATTN_TRACE); never loaded by the package
+TRACE_LIB = os.path.join(OUT_DIR, "libstreamindex_b200_trace.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -54,16 +57,17 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(d) <= t for d in _deps())
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
+    lib = TRACE_LIB if trace else LIB
+    if not force and not trace and up_to_date():
         return LIB
     nvcc = _nvcc()
-    obj_dir = os.path.join(OUT_DIR, "obj")
+    obj_dir = os.path.join(OUT_DIR, "obj_trace" if trace else "obj")
     os.makedirs(obj_dir, exist_ok=True)
 
     def compile_one(src):
         obj = os.path.join(obj_dir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc, *ARCH, *FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
+        cmd = [nvcc, *ARCH, *FLAGS, *(["-DSI_ATTN_TRACE"] if trace else []), "-I", INCLUDE, "-c", src, "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -75,18 +79,19 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
     with cf.ThreadPoolExecutor(max_workers=max(1, min(8, os.cpu_count() or 1))) as ex:
         objs = list(ex.map(compile_one, _sources()))
-    tmp = LIB + ".tmp"
+    tmp = lib + ".tmp"
     cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="build the SI_ATTN_TRACE debug library")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose, trace=a.trace))
