@@ -242,13 +242,14 @@ def load_traffic():
 
 
 def run_ours(a, world, rank, local):
-    from streamindex_b200.dist import balanced_bounds, broadcast_keys, gather_to_rank0, legal_pairs
+    from streamindex_b200.dist import (INDEXER_QUERY_COST_PAIRS, balanced_bounds, broadcast_keys, gather_to_rank0,
+                                       legal_pairs)
     from streamindex_b200.indexer import IndexerTopk, chunked_indexer_topk
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     T = a.S // a.ratio
-    bounds = balanced_bounds(a.S, world, T, a.ratio)
+    bounds = balanced_bounds(a.S, world, T, a.ratio, extra_per_query=INDEXER_QUERY_COST_PAIRS * a.H / 64)
     s_lo, s_hi = bounds[rank], bounds[rank + 1]
     n_loc = s_hi - s_lo
     q, k, w = gen_inputs(a, s_lo, s_hi, device, rank)

@@ -19,8 +19,10 @@
 //   3. dq[16 x D] += dp . kv: warp w owns D/4 columns, accumulated in registers
 //      across all tiles of the item;
 //   4. dkv[32 x D] = dp^T . q + p^T . do: warp w owns D/4 columns; each value
-//      is added to the fp32 dkv buffer with a vector reduction
-//      (red.global.add.v2.f32; the buffer is L2-resident at the benchmark sizes).
+//      is added to the fp32 dkv buffer with a 16-byte vector reduction
+//      (red.global.add.v4.f32: lane pairs swap half rows so each lane holds
+//      four consecutive columns of one row; the buffer is L2-resident at the
+//      benchmark sizes).
 // This is a correctness-first kernel on the warp-level MMA path (the reference
 // backward is forward-only territory for the north star); the forward is the
 // tcgen05 kernel.
@@ -70,8 +72,8 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
                : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
-__device__ __forceinline__ void red_add_v2(float* p, float a, float b) {
-  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
 __host__ __device__ inline int row_elems(int n) { return n + 8; }  // +16 B per row: conflict-free ldmatrix
@@ -241,14 +243,22 @@ __global__ void __launch_bounds__(kThreads) sparse_attn_bwd_kernel(Params p) {
             mma16816(acc[j], ap, bb);
           }
         }
-        const int k0 = mt * 16 + g, k1 = k0 + 8;
-        const int v0 = sIdx[k0], v1 = sIdx[k1];
-        float* d0 = v0 >= 0 ? p.dkv + ((size_t)b * p.Nkv + v0) * D + col0 + 2 * t4 : nullptr;
-        float* d1 = v1 >= 0 ? p.dkv + ((size_t)b * p.Nkv + v1) * D + col0 + 2 * t4 : nullptr;
+        // even lanes (t4 = 0, 2) add row k0, columns 2*t4 .. 2*t4+3; odd lanes add
+        // row k0+8, columns 2*(t4-1) .. +3 (each lane takes its partner's half)
+        const bool odd = t4 & 1;
+        const int kr = mt * 16 + g + (odd ? 8 : 0);
+        const int v = sIdx[kr];
+        float* dst = v >= 0 ? p.dkv + ((size_t)b * p.Nkv + v) * D + col0 + 2 * (t4 & ~1) : nullptr;
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
-          if (d0) red_add_v2(d0 + j * 8, acc[j][0], acc[j][1]);
-          if (d1) red_add_v2(d1 + j * 8, acc[j][2], acc[j][3]);
+          const float s0 = odd ? acc[j][0] : acc[j][2], s1 = odd ? acc[j][1] : acc[j][3];
+          const float r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+          if (dst) {
+            if (odd)
+              red_add_v4(dst + j * 8, r0, r1, acc[j][2], acc[j][3]);
+            else
+              red_add_v4(dst + j * 8, acc[j][0], acc[j][1], r0, r1);
+          }
         }
       }
     }

@@ -20,6 +20,15 @@ import torch
 import torch.distributed as dist
 
 
+# Fixed per-query cost of the fused indexer (selection, flushes, output write),
+# in units of causally legal (s, t) pairs at the large-S pair rate.  Fitted on
+# the single-GPU S sweep (H_I=64, D_I=128, k=512, T=S/4, S = 32K..1M): with
+# pairs = S^2/8, 1/frac = a + b/S gives b ~ 1.9e4, i.e. ~2.4k pairs per query
+# at the peak rate, ~1.8k at the large-S rate.  Balancing on pairs alone gives
+# rank 0 (the most, and shortest, queries) ~5% more time at 8 GPUs.
+INDEXER_QUERY_COST_PAIRS = 1800.0
+
+
 def legal_pairs(S: int, T: int, ratio: Optional[int], lo: int = 0, hi: Optional[int] = None) -> int:
     """Sum over s in [lo, hi) of min(T, (s+1)//ratio) (T per query without a ratio)."""
     hi = S if hi is None else hi
