@@ -696,95 +696,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t dst_off = (uint32_t)r * 128 + ((c ^ (uint32_t)(r & 7)) << 4);
     uint32_t st = 0, kph = 0, islot = 0, iph = 0;
     bool ok = true;
-    if constexpr (MODE == kFp8Rows) {
-      // FP8 rows, software-pipelined over the CTA's flattened (item, tile)
-      // sequence: the loads of the next tile's rows are in flight while this
-      // tile's rows are dequantised into the stage.  This thread loads 16-byte
-      // chunks qc = c + 8i of its row's e4m3 part (64-dim block qc/4 = stage
-      // atom qc/4), the scale of each of those blocks and rope chunk c.
-      struct Regs {
-        uint4 x[4];
-        uint4 rp;
-        float sc[4];
-      };
-      const int nq = p.n_nope >> 4;
-      auto fetch = [&](Regs& f, int it) -> bool {
-        if (!mbar_wait(&ms->idx_full[islot], iph, abort_flag, p.status, kErrWaitTmaFull)) return false;
-        const int row = ms->idx_ring[islot][r];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ms->idx_empty[islot]);
-        if (++islot == (uint32_t)kIdxSlots) {
-          islot = 0;
-          iph ^= 1;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          f.x[i] = make_uint4(0u, 0u, 0u, 0u);
-          f.sc[i] = 0.f;
-        }
-        f.rp = make_uint4(0u, 0u, 0u, 0u);
-        if (row >= 0) {
-          const uint8_t* rowp = kv_row_ptr_fp8(p, (it / p.hgroups) / p.S, row);
-          const float* scp = reinterpret_cast<const float*>(rowp + p.n_nope);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int qc = (int)c + 8 * i;
-            if (qc < nq) {
-              f.x[i] = __ldg(reinterpret_cast<const uint4*>(rowp) + qc);
-              f.sc[i] = __ldg(scp + (qc >> 2));
-            }
-          }
-          if ((int)c * 8 < p.D - p.n_nope) f.rp = __ldg(reinterpret_cast<const uint4*>(rowp + p.rope_off) + c);
-        }
-        return true;
-      };
-      auto commit = [&](const Regs& f) -> bool {
-        if (!mbar_wait(&ms->kv_empty[st], kph ^ 1, abort_flag, p.status, kErrWaitTmaEmpty)) return false;
-        uint8_t* stg = sKV + (size_t)st * SB;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int qc = (int)c + 8 * i;
-          if (qc < nq) {
-            uint4 lo, hi;
-            dequant16_e4m3(f.x[i], f.sc[i], lo, hi);
-            const int a = qc >> 2, ch = 2 * (qc & 3);
-            *reinterpret_cast<uint4*>(stg + stage_off<NK>(a, r, ch)) = lo;
-            *reinterpret_cast<uint4*>(stg + stage_off<NK>(a, r, ch + 1)) = hi;
-          }
-        }
-        *reinterpret_cast<uint4*>(stg + stage_off<NK>(p.n_nope >> 6, r, (int)c)) = f.rp;
-        fence_proxy_async_smem();
-        mbar_arrive(&ms->kv_full[st]);
-        if (++st == (uint32_t)NST) {
-          st = 0;
-          kph ^= 1;
-        }
-        return true;
-      };
-      auto advance = [&](int& it, int& t) {
-        if (++t == ntiles) {
-          t = 0;
-          it += (int)gridDim.x;
-        }
-      };
-      Regs ra, rb;
-      int it = blockIdx.x, t = 0;
-      ok = it < nitems && fetch(ra, it);
-      while (ok) {  // unrolled by two so the register buffers are named statically
-        int it2 = it, t2 = t;
-        advance(it2, t2);
-        const bool more = it2 < nitems;
-        if ((more && !fetch(rb, it2)) || !commit(ra) || !more) break;
-        it = it2;
-        t = t2;
-        advance(it2, t2);
-        const bool more2 = it2 < nitems;
-        if ((more2 && !fetch(ra, it2)) || !commit(rb) || !more2) break;
-        it = it2;
-        t = t2;
-      }
-      ok = false;  // the bf16 loop below is skipped
-    }
     for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
       const int bs = it / p.hgroups;
       const int b = bs / p.S;
@@ -811,6 +722,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         SI_TRACE_IF(tr, 0, ii, t, 1);
+        if (MODE == kFp8Rows) {
+          // FP8 rows: this thread loads 16-byte chunks q = c + 8i of the row's
+          // e4m3 part (64-dim block q/4 = atom q/4), the row's block scales and
+          // rope chunk c, then writes the dequantised bf16 chunks into the stage.
+          uint4 x[4] = {}, rp = make_uint4(0u, 0u, 0u, 0u);
+          float4 sc0 = make_float4(0.f, 0.f, 0.f, 0.f), sc1 = sc0;
+          const int nq = p.n_nope >> 4;
+          if (vld) {
+            const uint8_t* rowp = kv_row_ptr_fp8(p, b, row);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int qc = (int)c + 8 * i;
+              if (qc < nq) x[i] = __ldg(reinterpret_cast<const uint4*>(rowp) + qc);
+            }
+            sc0 = __ldg(reinterpret_cast<const float4*>(rowp + p.n_nope));
+            if (p.n_nope > 256) sc1 = __ldg(reinterpret_cast<const float4*>(rowp + p.n_nope) + 1);
+            if ((int)c * 8 < p.D - p.n_nope) rp = __ldg(reinterpret_cast<const uint4*>(rowp + p.rope_off) + c);
+          }
+          uint8_t* stg = sKV + (size_t)st * SB;
+          const float scs[8] = {sc0.x, sc0.y, sc0.z, sc0.w, sc1.x, sc1.y, sc1.z, sc1.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int qc = (int)c + 8 * i;
+            if (qc < nq) {
+              uint4 lo, hi;
+              // block qc/4 = 2i + (c >= 4): static indices, no local-memory array
+              dequant16_e4m3(x[i], (c >= 4) ? scs[2 * i + 1] : scs[2 * i], lo, hi);
+              const int a = qc >> 2, ch = 2 * (qc & 3);
+              *reinterpret_cast<uint4*>(stg + stage_off<NK>(a, r, ch)) = lo;
+              *reinterpret_cast<uint4*>(stg + stage_off<NK>(a, r, ch + 1)) = hi;
+            }
+          }
+          *reinterpret_cast<uint4*>(stg + stage_off<NK>(p.n_nope >> 6, r, (int)c)) = rp;
+          fence_proxy_async_smem();
+          mbar_arrive(&ms->kv_full[st]);
+          if (++st == (uint32_t)NST) {
+            st = 0;
+            kph ^= 1;
+          }
+          continue;
+        }
         const uint32_t base = smem_u32(sKV + (size_t)st * SB) + dst_off;
         const __nv_bfloat16* src = (vld ? kv_row_ptr(p, b, row) : p.kv) + c * 8;
 #pragma unroll
