@@ -24,8 +24,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OUT_DIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(OUT_DIR, "libstreamindex_b200.so")
-# debug build of the same sources with the attention kernel's per-tile
-# %globaltimer stamps compiled in (SI_ATTN_TRACE); never loaded by the package
+# debug build of the same sources with the kernels' per-tile %globaltimer
+# stamps compiled in (SI_ATTN_TRACE, SI_IDX_TRACE); never loaded by the package
 TRACE_LIB = os.path.join(OUT_DIR, "libstreamindex_b200_trace.so")
 INCLUDE = os.path.join(ROOT, "include")
 
@@ -67,7 +67,7 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> st
 
     def compile_one(src):
         obj = os.path.join(obj_dir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc, *ARCH, *FLAGS, *(["-DSI_ATTN_TRACE"] if trace else []), "-I", INCLUDE, "-c", src, "-o", obj]
+        cmd = [nvcc, *ARCH, *FLAGS, *(["-DSI_ATTN_TRACE", "-DSI_IDX_TRACE"] if trace else []), "-I", INCLUDE, "-c", src, "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -92,6 +92,6 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
-    ap.add_argument("--trace", action="store_true", help="build the SI_ATTN_TRACE debug library")
+    ap.add_argument("--trace", action="store_true", help="build the per-tile trace debug library")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose, trace=a.trace))

@@ -184,3 +184,46 @@ def test_indexer_fp16_operands():
     gi, gv = si.chunked_indexer_topk(q16.cuda(), k16.cuda(), w.cuda(), 24, causal_ratio=4)
     oi, ov = oracle.materialize_topk(q16, k16, w, 24, ratio=4)
     assert_topk_exact_up_to_ties(q16, k16, w, gi.cpu(), gv.cpu(), oi, ov)
+
+
+def test_exact_ties_prefer_smaller_index():
+    """Exact score ties resolve toward the smaller key index
+    (docs/streaming_topk.md:48-66, 301-305): keys 32..63 duplicate keys 0..31,
+    so every score occurs twice; whenever key j >= 32 is selected, key j - 32
+    must be selected too and placed before it."""
+    import streamindex_b200 as si
+
+    q, kk, w = oracle.indexer_inputs(1, 200, 64, 128, 64, seed=71)
+    kk[:, 32:] = kk[:, :32]
+    gi, gv = si.chunked_indexer_topk(q.cuda(), kk.cuda(), w.cuda(), 40, causal_ratio=None)
+    gi, gv = gi.cpu(), gv.cpu()
+    for s in range(gi.shape[1]):
+        row = gi[0, s].tolist()
+        pos = {t: i for i, t in enumerate(row)}
+        for t in row:
+            if t >= 32:
+                assert t - 32 in pos and pos[t - 32] < pos[t], (s, t)
+                assert gv[0, s, pos[t]] == gv[0, s, pos[t - 32]]
+    oi, ov = oracle.materialize_topk(q, kk, w, 40)
+    assert_topk_exact_up_to_ties(q, kk, w, gi, gv, oi, ov)
+
+
+def test_sharded_slices_equal_whole_sequence():
+    """The S-sharded indexer (work-balanced contiguous slices with a global
+    query offset, as each rank runs them) concatenates to the single-call
+    result bit for bit; chunk_s / chunk_t do not change results."""
+    import streamindex_b200 as si
+    from streamindex_b200.dist import INDEXER_QUERY_COST_PAIRS, balanced_bounds
+    from streamindex_b200.indexer import indexer_topk_slice
+
+    S, H, D, T, k = 4096, 64, 128, 1024, 256
+    q, kk, w = oracle.indexer_inputs(2, S, H, D, T, seed=72)
+    q, kk, w = q.cuda(), kk.cuda(), w.cuda()
+    full_i, full_v = si.chunked_indexer_topk(q, kk, w, k, causal_ratio=4)
+    alt_i, alt_v = si.chunked_indexer_topk(q, kk, w, k, causal_ratio=4, chunk_s=512, chunk_t=128)
+    assert torch.equal(full_i, alt_i) and torch.equal(full_v, alt_v)
+    bounds = balanced_bounds(S, 5, T, 4, extra_per_query=INDEXER_QUERY_COST_PAIRS)
+    parts = [indexer_topk_slice(q[:, a:b], kk, w[:, a:b], k, 4, a) for a, b in zip(bounds, bounds[1:])]
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat([p[0] for p in parts], dim=1), full_i)
+    assert torch.equal(torch.cat([p[1] for p in parts], dim=1), full_v)
