@@ -19,9 +19,10 @@
 // double buffer: the epilogue of group 0 overlaps the MMAs of group 1.
 //
 // Warp roles (576 threads for H_I <= 64, 320 for H_I = 128):
-//   warp 0      TMA producer (Q block, K tiles; q is a 4-D [B,S,H,D] and k a 3-D
-//               [B,T,D] tensor map, so any strides with a contiguous last dim
-//               are read in place)
+//   warp 0      TMA producer (Q block, K tiles; q and k are 2-D [rows, D] tensor
+//               maps when their rows are evenly spaced, else 4-D [B,S,H,D] /
+//               3-D [B,T,D] maps, so any strides with a contiguous last dim are
+//               read in place)
 //   warp 1      TMEM allocator + single-thread UMMA issuer
 //   warps 2..   epilogue: scores + streaming top-k.  Warp w reads TMEM lanes
 //               32*(w%4)..+32 (its "quadrant"); the epilogue warps are cut into
@@ -86,7 +87,6 @@ struct IndexerParams {
   int* status;                // device status word
   int nblk_per_batch;         // ceil(S / QC)
   long long s_offset;         // global position of local query 0 (causal mask uses s_offset + s)
-  long long w_sb, w_ss, w_sh;  // element strides of w over (b, s, h)
   unsigned long long* trace;  // debug builds (SI_IDX_TRACE) only
 };
 
