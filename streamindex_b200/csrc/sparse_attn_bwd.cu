@@ -10,22 +10,22 @@
 //   dsink[h] = -sum_queries exp(sink[h] - lse[h]) * delta[h]
 // As in the reference, p and dp enter the products rounded to the operand type.
 //
-// Mapping.  A work item is one query (b, s) and a group of 16 heads (the M of
-// the warp-level bf16 MMA, mma.sync m16n8k16).  Four warps; per 32-key tile:
-//   1. the tile's kv rows are gathered into shared memory (cp.async; masked
-//      slots zero-filled);
-//   2. warp w computes S and dO.V^T for keys [8w, 8w+8) (K = D and Dv), then
-//      p and dp in registers, written to shared memory in bf16;
-//   3. dq[16 x D] += dp . kv: warp w owns D/4 columns, accumulated in registers
-//      across all tiles of the item;
-//   4. dkv[32 x D] = dp^T . q + p^T . do: warp w owns D/4 columns; each value
-//      is added to the fp32 dkv buffer with a 16-byte vector reduction
-//      (red.global.add.v4.f32: lane pairs swap half rows so each lane holds
-//      four consecutive columns of one row; the buffer is L2-resident at the
-//      benchmark sizes).
-// This is a correctness-first kernel on the warp-level MMA path (the reference
-// backward is forward-only territory for the north star); the forward is the
-// tcgen05 kernel.
+// Mapping.  A work item is one query (b, s) and a group of 64 heads (four
+// m16 tiles of the warp-level bf16 MMA, mma.sync m16n8k16), so every selected
+// kv row is gathered once per query and its dkv contribution is summed over
+// all 64 heads before it reaches global memory.  16 warps; the rows of tile
+// t+1 are gathered (cp.async, masked slots zero-filled) while tile t computes:
+//   1. S and dO.V^T: warp w owns heads 16*(w%4).. and keys 8*(w/4)..; p and dp
+//      in registers, written to shared memory in bf16;
+//   2. dq[64 x D] += dp . kv: warp w owns 16 heads x D/4 columns,
+//      accumulated in registers across all tiles of the item;
+//   3. dkv[32 x D] = dp^T . q + p^T . do (contraction over the 64 heads):
+//      warp w owns 16 keys x D/8 columns; each value is added to the fp32 dkv
+//      buffer with a 16-byte vector reduction (red.global.add.v4.f32: lane
+//      pairs swap half rows so each lane holds four consecutive columns of one
+//      row; the buffer is L2-resident at the benchmark sizes).
+// The backward runs on the warp-level MMA path; the forward is the tcgen05
+// kernel.
 #include <cuda_bf16.h>
 
 #include "capi_common.h"
@@ -35,10 +35,11 @@
 namespace si {
 namespace attn_bwd {
 
-constexpr int kHeads = 16;   // MMA M
+constexpr int kHeads = 64;   // heads per work item (4 m16 tiles)
 constexpr int kKeys = 32;    // keys per tile
-constexpr int kWarps = 4;
+constexpr int kWarps = 16;
 constexpr int kThreads = 32 * kWarps;
+constexpr int kMaxSmem = 232448;
 
 struct Params {
   int B, S, H, D, Dv, Nkv, K;
@@ -66,72 +67,138 @@ __device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t (&r)[2]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
 }
 // C[16x8] += A[16x16] . B[16x8], bf16 in, fp32 accumulate.
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
                "{%0,%1,%2,%3};"
                : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-__host__ __device__ inline int row_elems(int n) { return n + 8; }  // +16 B per row: conflict-free ldmatrix
-
-__host__ __device__ inline size_t smem_bytes(int D, int Dv) {
-  return (size_t)2 * (kHeads * row_elems(D) + kHeads * row_elems(Dv) + kKeys * row_elems(D) +
-                      2 * kHeads * row_elems(kKeys)) +
-         sizeof(float) * 2 * kHeads + sizeof(int) * kKeys + 64;
+// 32 TMEM lanes x 8 fp32 columns (thread i: lane base + i), load + wait in one asm.
+__device__ __forceinline__ void tmem_ld8_sync(uint32_t taddr, float (&v)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "f"(v[0]),
+               "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
 }
 
-// NT = D / 32: n8 tiles per warp over its quarter of the D columns.
+__host__ __device__ inline int row_elems(int n) { return n + 8; }  // +16 B per row: conflict-free ldmatrix
+
+__host__ __device__ inline size_t smem_bytes(int D, int Dv, int nst) {
+  return (size_t)2 * (kHeads * row_elems(D) + kHeads * row_elems(Dv) + (size_t)nst * kKeys * row_elems(D) +
+                      2 * kHeads * row_elems(kKeys)) +
+         sizeof(float) * 2 * kHeads + sizeof(int) * 2 * kKeys + 64 + 16;
+}
+// Two kv stages (the next tile's gather overlaps this tile's math) when they fit.
+__host__ __device__ inline int kv_stages(int D, int Dv) { return smem_bytes(D, Dv, 2) <= (size_t)kMaxSmem ? 2 : 1; }
+
+// NT = D / 32: n8 tiles of a warp's dq columns (D/4); D/64 of its dkv columns (D/8).
 template <int NT>
-__global__ void __launch_bounds__(kThreads) sparse_attn_bwd_kernel(Params p) {
+__global__ void __launch_bounds__(kThreads, 1) sparse_attn_bwd_kernel(Params p) {
   extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int NTK = NT / 2;
   const int D = p.D, Dv = p.Dv;
   const int LQ = row_elems(D), LO = row_elems(Dv), LP = row_elems(kKeys);
+  const int nst = kv_stages(D, Dv);
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* sDO = sQ + kHeads * LQ;
   __nv_bfloat16* sKV = sDO + kHeads * LO;
-  __nv_bfloat16* sP = sKV + kKeys * LQ;
+  __nv_bfloat16* sP = sKV + nst * kKeys * LQ;
   __nv_bfloat16* sDS = sP + kHeads * LP;
   float* sLse = reinterpret_cast<float*>(sDS + kHeads * LP);
   float* sDelta = sLse + kHeads;
-  int* sIdx = reinterpret_cast<int*>(sDelta + kHeads);
+  int* sIdx = reinterpret_cast<int*>(sDelta + kHeads);  // [2][kKeys]
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(sIdx + 2 * kKeys);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
+  const int hm = warp & 3;   // head tile of phases 1 and 2
   const int hgroups = (p.H + kHeads - 1) / kHeads;
   const long long nitems = (long long)p.B * p.S * hgroups;
   const int ntiles = (p.K + kKeys - 1) / kKeys;
-  const int CW = D / 4;  // columns per warp (NT n8 tiles)
+  const int chunks = D / 8;  // 16-byte chunks per kv / q row
+  // dq lives in tensor memory between tiles (72 fp32 per thread at D=576 would
+  // otherwise pin registers the three products need): warp w owns lanes
+  // 32*(w%4).., columns (w/4)*4*NT.., one column per fp32 value of its
+  // m16n8 fragments (tile j at columns 4j..4j+3).
+  constexpr uint32_t kTmemCols = NT * 16 <= 32 ? 32 : NT * 16 <= 64 ? 64 : NT * 16 <= 128 ? 128 : NT * 16 <= 256 ? 256 : 512;
+  if (warp == 0) {
+    tmem_alloc(sTmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tdq = *sTmem + ((uint32_t)(32 * hm) << 16) + (uint32_t)((warp >> 2) * 4 * NT);
+
+  // cp.async of one tile's kv rows into a stage, indices read from global memory
+  auto gather = [&](const int* irow, int b, int t, __nv_bfloat16* stage, int* sidx) {
+    if (tid < kKeys) {
+      const int kk = t * kKeys + tid;
+      const int v = kk < p.K ? irow[kk] : -1;
+      sidx[tid] = (v >= 0 && v < p.Nkv) ? v : -1;
+    }
+    for (int i = tid; i < kKeys * chunks; i += kThreads) {
+      const int r = i / chunks, c = i % chunks;
+      const int kk = t * kKeys + r;
+      int v = kk < p.K ? __ldg(irow + kk) : -1;
+      v = (v >= 0 && v < p.Nkv) ? v : -1;
+      const __nv_bfloat16* src = v >= 0 ? p.kv + ((size_t)b * p.Nkv + v) * D + c * 8 : p.kv;
+      cp_async_16(smem_u32(stage + r * LQ + c * 8), src, v >= 0 ? 16u : 0u);
+    }
+  };
 
   for (long long it = blockIdx.x; it < nitems; it += gridDim.x) {
     const int hg = (int)(it % hgroups);
     const long long bs = it / hgroups;
     const int b = (int)(bs / p.S);
     const int h0 = hg * kHeads;
-    // ---- q, do rows of the 16 heads (zero rows past H), lse, delta, dsink
-    for (int i = tid; i < kHeads * (D / 8); i += kThreads) {
-      const int r = i / (D / 8), c = i % (D / 8);
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (h0 + r < p.H) v = *reinterpret_cast<const uint4*>(p.q + ((size_t)bs * p.H + h0 + r) * D + c * 8);
-      *reinterpret_cast<uint4*>(sQ + r * LQ + c * 8) = v;
+    const int* irow = p.idx + (size_t)bs * p.K;
+    __syncthreads();  // the previous item is done with every shared tile
+    // ---- q, do rows of the 64 heads (zero rows past H)
+    for (int i = tid; i < kHeads * chunks; i += kThreads) {
+      const int r = i / chunks, c = i % chunks;
+      const bool ok = h0 + r < p.H;
+      cp_async_16(smem_u32(sQ + r * LQ + c * 8), ok ? p.q + ((size_t)bs * p.H + h0 + r) * D + c * 8 : p.q, ok ? 16u : 0u);
     }
     for (int i = tid; i < kHeads * (Dv / 8); i += kThreads) {
       const int r = i / (Dv / 8), c = i % (Dv / 8);
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (h0 + r < p.H) v = *reinterpret_cast<const uint4*>(p.dout + ((size_t)bs * p.H + h0 + r) * Dv + c * 8);
-      *reinterpret_cast<uint4*>(sDO + r * LO + c * 8) = v;
+      const bool ok = h0 + r < p.H;
+      cp_async_16(smem_u32(sDO + r * LO + c * 8), ok ? p.dout + ((size_t)bs * p.H + h0 + r) * Dv + c * 8 : p.dout,
+                  ok ? 16u : 0u);
     }
+    cp_async_commit();
+    if (nst == 2) gather(irow, b, 0, sKV, sIdx);
+    cp_async_commit();
+    // ---- delta = o . do, lse and dsink: four heads per warp (o read from global memory)
 #pragma unroll 1
-    for (int r = warp; r < kHeads; r += kWarps) {  // delta: one warp per head row
+    for (int r = warp; r < kHeads; r += kWarps) {
       const int h = h0 + r;
       float acc = 0.f;
       if (h < p.H) {
         const __nv_bfloat16* orow = p.o + ((size_t)bs * p.H + h) * Dv;
         const __nv_bfloat16* drow = p.dout + ((size_t)bs * p.H + h) * Dv;
-        for (int d = lane; d < Dv; d += 32) acc += __bfloat162float(orow[d]) * __bfloat162float(drow[d]);
+        for (int d = lane * 8; d < Dv; d += 256) {
+          const uint4 ov = *reinterpret_cast<const uint4*>(orow + d);
+          const uint4 dv = *reinterpret_cast<const uint4*>(drow + d);
+          const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+          const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 a = __bfloat1622float2(o2[e]), c = __bfloat1622float2(d2[e]);
+            acc += a.x * c.x + a.y * c.y;
+          }
+        }
       }
 #pragma unroll
       for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
@@ -143,57 +210,64 @@ __global__ void __launch_bounds__(kThreads) sparse_attn_bwd_kernel(Params p) {
       }
     }
 
-    float dq[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) dq[j][0] = dq[j][1] = dq[j][2] = dq[j][3] = 0.f;
-
-    const int* irow = p.idx + (size_t)bs * p.K;
 #pragma unroll 1
     for (int t = 0; t < ntiles; ++t) {
-      __syncthreads();  // previous tile's shared tiles are free; q/do/lse/delta visible
-      if (tid < kKeys) {
-        const int kk = t * kKeys + tid;
-        const int v = kk < p.K ? irow[kk] : -1;
-        sIdx[tid] = (v >= 0 && v < p.Nkv) ? v : -1;
+      __nv_bfloat16* stage = sKV + (nst == 2 ? (t & 1) : 0) * kKeys * LQ;
+      const int* sid = sIdx + (nst == 2 ? (t & 1) : 0) * kKeys;
+      if (nst == 2) {
+        if (t + 1 < ntiles) gather(irow, b, t + 1, sKV + ((t + 1) & 1) * kKeys * LQ, sIdx + ((t + 1) & 1) * kKeys);
+        cp_async_commit();
+        cp_async_wait<1>();
+      } else {
+        gather(irow, b, t, stage, sIdx);
+        cp_async_commit();
+        cp_async_wait<0>();
       }
-      __syncthreads();
-      for (int i = tid; i < kKeys * (D / 8); i += kThreads) {
-        const int r = i / (D / 8), c = i % (D / 8);
-        const int v = sIdx[r];
-        const __nv_bfloat16* src = v >= 0 ? p.kv + ((size_t)b * p.Nkv + v) * D + c * 8 : p.kv;
-        cp_async_16(smem_u32(sKV + r * LQ + c * 8), src, v >= 0 ? 16u : 0u);
-      }
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
+      __syncthreads();  // tile t (and, at t = 0, q / do / delta) visible to all warps
 
-      // ---- S and dO.V^T for keys [8w, 8w+8)
+      // ---- 1. S and dO.V^T for heads 16*hm.., keys 8*(warp/4)..
       {
+        // S over D and dO.V^T over Dv share the kv fragment of each k step;
+        // two accumulator chains each (even / odd k) halve the MMA dependency chain
         float s[4] = {0.f, 0.f, 0.f, 0.f}, dpv[4] = {0.f, 0.f, 0.f, 0.f};
-        const int n0 = 8 * warp;
-        const uint32_t a_q = smem_u32(sQ + (lane & 15) * LQ + (lane >> 4) * 8);
-        const uint32_t a_o = smem_u32(sDO + (lane & 15) * LO + (lane >> 4) * 8);
-        const uint32_t b_kv = smem_u32(sKV + (n0 + (lane & 7)) * LQ + ((lane >> 3) & 1) * 8);
+        float s2[4] = {0.f, 0.f, 0.f, 0.f}, dpv2[4] = {0.f, 0.f, 0.f, 0.f};
+        const int n0 = 8 * (warp >> 2);
+        const uint32_t a_q = smem_u32(sQ + (hm * 16 + (lane & 15)) * LQ + (lane >> 4) * 8);
+        const uint32_t a_o = smem_u32(sDO + (hm * 16 + (lane & 15)) * LO + (lane >> 4) * 8);
+        // lanes 16-31 address the next k step (x4 loads: two k steps' fragments)
+        const uint32_t b_kv = smem_u32(stage + (n0 + (lane & 7)) * LQ + ((lane >> 3) & 1) * 8 + (lane >> 4) * 16);
+        const int kv2 = Dv / 32;  // k-step pairs shared by both products
+#pragma unroll 2
+        for (int k2 = 0; k2 < kv2; ++k2) {
+          uint32_t a[4], c[4], bb[4];
+          ldsm_x4(b_kv + k2 * 64, bb);  // k steps 2*k2 (bb[0..1]) and 2*k2+1 (bb[2..3])
+          ldsm_x4(a_q + k2 * 64, a);
+          ldsm_x4(a_o + k2 * 64, c);
+          mma16816(s, a, bb[0], bb[1]);
+          mma16816(dpv, c, bb[0], bb[1]);
+          ldsm_x4(a_q + k2 * 64 + 32, a);
+          ldsm_x4(a_o + k2 * 64 + 32, c);
+          mma16816(s2, a, bb[2], bb[3]);
+          mma16816(dpv2, c, bb[2], bb[3]);
+        }
 #pragma unroll 4
-        for (int k = 0; k < D / 16; ++k) {
+        for (int k = 2 * kv2; k < D / 16; ++k) {  // the q.k dims past Dv
           uint32_t a[4], bb[2];
           ldsm_x4(a_q + k * 32, a);
           ldsm_x2(b_kv + k * 32, bb);
-          mma16816(s, a, bb);
+          mma16816(s, a, bb[0], bb[1]);
         }
-#pragma unroll 4
-        for (int k = 0; k < Dv / 16; ++k) {
-          uint32_t a[4], bb[2];
-          ldsm_x4(a_o + k * 32, a);
-          ldsm_x2(b_kv + k * 32, bb);
-          mma16816(dpv, a, bb);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s[e] += s2[e];
+          dpv[e] += dpv2[e];
         }
-        // thread values: heads g, g+8; keys n0 + 2*t4, +1
+        // thread values: heads 16*hm + g (+8); keys n0 + 2*t4 (+1)
         const int c0 = n0 + 2 * t4;
-        const bool v0 = sIdx[c0] >= 0, v1 = sIdx[c0 + 1] >= 0;
+        const bool v0 = sid[c0] >= 0, v1 = sid[c0 + 1] >= 0;
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
-          const int r = g + 8 * hr;
+          const int r = hm * 16 + g + 8 * hr;
           const bool hv = h0 + r < p.H;
           const float lse = sLse[r], dl = sDelta[r];
           const float p0 = (hv && v0) ? expf(s[2 * hr] * p.scale - lse) : 0.f;
@@ -206,80 +280,125 @@ __global__ void __launch_bounds__(kThreads) sparse_attn_bwd_kernel(Params p) {
       }
       __syncthreads();
 
-      const int col0 = warp * CW;
-      // ---- dq += dS . kv   (A = dS [16 x 32], B = kv [32 keys x D] row-major -> trans loads)
+      // ---- 2. dq += dS . kv  (A = dS [16 heads x 32 keys], B = kv [32 keys x D/4] via trans loads),
+      // two n8 tiles at a time through tensor memory
+      {
+        const int col0 = (warp >> 2) * (D / 4);
+        uint32_t a0[4], a1[4];
+        ldsm_x4(smem_u32(sDS + (hm * 16 + (lane & 15)) * LP + (lane >> 4) * 8), a0);
+        ldsm_x4(smem_u32(sDS + (hm * 16 + (lane & 15)) * LP + 16 + (lane >> 4) * 8), a1);
+        const uint32_t b0 = smem_u32(stage + (lane & 15) * LQ + col0 + (lane >> 4) * 8);
+        const uint32_t b1 = b0 + 16 * LQ * 2;
+#pragma unroll 3
+        for (int j = 0; j < NT; j += 2) {
+          float v[8];
+          if (t == 0) {
 #pragma unroll
-      for (int ks = 0; ks < kKeys / 16; ++ks) {
-        uint32_t a[4];
-        ldsm_x4(smem_u32(sDS + (lane & 15) * LP + ks * 16 + (lane >> 4) * 8), a);
-        const uint32_t b_base = smem_u32(sKV + (ks * 16 + (lane & 15)) * LQ + col0);
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          uint32_t bb[2];
-          ldsm_x2_t(b_base + j * 16, bb);
-          mma16816(dq[j], a, bb);
-        }
-      }
-      // ---- dkv[32 x D] = dS^T . q + P^T . do, one 16-key half at a time
-#pragma unroll 1
-      for (int mt = 0; mt < kKeys / 16; ++mt) {
-        float acc[NT][4];
-#pragma unroll
-        for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-        // A = X^T with X [16 heads x 32 keys]: transposed 8x8 blocks
-        const int arow = (lane >> 4) * 8 + (lane & 7), acol = mt * 16 + ((lane >> 3) & 1) * 8;
-        uint32_t ads[4], ap[4];
-        ldsm_x4_t(smem_u32(sDS + arow * LP + acol), ads);
-        ldsm_x4_t(smem_u32(sP + arow * LP + acol), ap);
-        const uint32_t bq = smem_u32(sQ + (lane & 15) * LQ + col0);
-        const uint32_t bo = smem_u32(sDO + (lane & 15) * LO + col0);
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          uint32_t bb[2];
-          ldsm_x2_t(bq + j * 16, bb);
-          mma16816(acc[j], ads, bb);
-          if (col0 + j * 8 < Dv) {
-            ldsm_x2_t(bo + j * 16, bb);
-            mma16816(acc[j], ap, bb);
+            for (int e = 0; e < 8; ++e) v[e] = 0.f;
+          } else {
+            tmem_ld8_sync(tdq + 4 * j, v);
           }
+          float(&c0)[4] = *reinterpret_cast<float(*)[4]>(v);
+          float(&c1)[4] = *reinterpret_cast<float(*)[4]>(v + 4);
+          uint32_t bb[4], bc[4];
+          ldsm_x4_t(b0 + j * 16, bb);
+          ldsm_x4_t(b1 + j * 16, bc);
+          mma16816(c0, a0, bb[0], bb[1]);
+          mma16816(c1, a0, bb[2], bb[3]);
+          mma16816(c0, a1, bc[0], bc[1]);
+          mma16816(c1, a1, bc[2], bc[3]);
+          tmem_st8(tdq + 4 * j, v);
         }
+        tmem_st_wait();
+      }
+      // ---- 3. dkv[16 keys x D/8] = dS^T . q + P^T . do, contraction over the 64 heads
+      {
+        const int km = warp & 1, colc = (warp >> 1) * (D / 8);
+        const int arow = (lane >> 4) * 8 + (lane & 7), acol = km * 16 + ((lane >> 3) & 1) * 8;
         // even lanes (t4 = 0, 2) add row k0, columns 2*t4 .. 2*t4+3; odd lanes add
         // row k0+8, columns 2*(t4-1) .. +3 (each lane takes its partner's half)
         const bool odd = t4 & 1;
-        const int kr = mt * 16 + g + (odd ? 8 : 0);
-        const int v = sIdx[kr];
-        float* dst = v >= 0 ? p.dkv + ((size_t)b * p.Nkv + v) * D + col0 + 2 * (t4 & ~1) : nullptr;
+        const int v = sid[km * 16 + g + (odd ? 8 : 0)];
+        float* dst = v >= 0 ? p.dkv + ((size_t)b * p.Nkv + v) * D + colc + 2 * (t4 & ~1) : nullptr;
+        // columns in chunks of at most CH n8 tiles (bounds the accumulator registers
+        // that are live beside the dq accumulators)
+        constexpr int CH = NTK > 5 ? (NTK + 1) / 2 : NTK;
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const float s0 = odd ? acc[j][0] : acc[j][2], s1 = odd ? acc[j][1] : acc[j][3];
-          const float r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
-          if (dst) {
-            if (odd)
-              red_add_v4(dst + j * 8, r0, r1, acc[j][2], acc[j][3]);
-            else
-              red_add_v4(dst + j * 8, acc[j][0], acc[j][1], r0, r1);
+        for (int j0 = 0; j0 < NTK; j0 += CH) {
+          float acc[CH][4];
+#pragma unroll
+          for (int j = 0; j < CH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+#pragma unroll
+          for (int kh = 0; kh < kHeads / 16; ++kh) {
+            // A = X^T with X [16 heads x 16 keys]: transposed 8x8 blocks
+            uint32_t ads[4], ap[4];
+            ldsm_x4_t(smem_u32(sDS + (kh * 16 + arow) * LP + acol), ads);
+            ldsm_x4_t(smem_u32(sP + (kh * 16 + arow) * LP + acol), ap);
+            const uint32_t bq = smem_u32(sQ + (kh * 16 + (lane & 15)) * LQ + colc);
+            const uint32_t bo = smem_u32(sDO + (kh * 16 + (lane & 15)) * LO + colc);
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const int jj = j0 + j;
+              if (jj < NTK) {
+                uint32_t bb[2];
+                ldsm_x2_t(bq + jj * 16, bb);
+                mma16816(acc[j], ads, bb[0], bb[1]);
+                if (colc + jj * 8 < Dv) {
+                  ldsm_x2_t(bo + jj * 16, bb);
+                  mma16816(acc[j], ap, bb[0], bb[1]);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const int jj = j0 + j;
+            const float s0 = odd ? acc[j][0] : acc[j][2], s1 = odd ? acc[j][1] : acc[j][3];
+            const float r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+            if (dst && jj < NTK) {
+              if (odd)
+                red_add_v4(dst + jj * 8, r0, r1, acc[j][2], acc[j][3]);
+              else
+                red_add_v4(dst + jj * 8, acc[j][0], acc[j][1], r0, r1);
+            }
           }
         }
       }
+      __syncthreads();  // stage t and sP / sDS free for the next tile
     }
-    // ---- dq out (rows g, g+8; columns col0 + 8j + 2*t4)
-    const int col0 = warp * CW;
+    // ---- dq out (heads 16*hm + g (+8); columns col0 + 8j + 2*t4)
+    const int col0 = (warp >> 2) * (D / 4);
+#pragma unroll 1
+    for (int j = 0; j < NT; j += 2) {
+      float v[8];
+      if (ntiles > 0) {
+        tmem_ld8_sync(tdq + 4 * j, v);
+      } else {
 #pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      const int h = h0 + g + 8 * hr;
-      if (h >= p.H) continue;
-      __nv_bfloat16* drow = p.dq + ((size_t)bs * p.H + h) * D + col0 + 2 * t4;
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
 #pragma unroll
-      for (int j = 0; j < NT; ++j)
-        *reinterpret_cast<uint32_t*>(drow + j * 8) = pack_bf16x2(dq[j][2 * hr], dq[j][2 * hr + 1]);
+      for (int hr = 0; hr < 2; ++hr) {
+        const int h = h0 + hm * 16 + g + 8 * hr;
+        if (h >= p.H) continue;
+        __nv_bfloat16* drow = p.dq + ((size_t)bs * p.H + h) * D + col0 + 2 * t4;
+        *reinterpret_cast<uint32_t*>(drow + j * 8) = pack_bf16x2(v[2 * hr], v[2 * hr + 1]);
+        *reinterpret_cast<uint32_t*>(drow + j * 8 + 8) = pack_bf16x2(v[4 + 2 * hr], v[4 + 2 * hr + 1]);
+      }
     }
-    __syncthreads();
+  }
+  cp_async_wait<0>();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(*sTmem, kTmemCols);
   }
 }
 
 template <int NT>
 static cudaError_t launch_nt(const Params& p, int grid, cudaStream_t stream) {
-  const size_t smem = smem_bytes(p.D, p.Dv);
+  const size_t smem = smem_bytes(p.D, p.Dv, kv_stages(p.D, p.Dv));
   static unsigned long long configured = 0;
   cudaError_t e = set_smem_attr_once(reinterpret_cast<const void*>(sparse_attn_bwd_kernel<NT>), (int)smem, &configured);
   if (e != cudaSuccess) return e;
@@ -319,7 +438,7 @@ int si_sparse_attn_bwd(const void* q, const void* kv, const float* attn_sink, co
   p.dkv = dkv_f32;
   p.dsink = dsink;
   const long long items = (long long)B * S * ((H + attn_bwd::kHeads - 1) / attn_bwd::kHeads);
-  const long long cap = (long long)device_sm_count() * 2;
+  const long long cap = (long long)device_sm_count();
   const int grid = (int)(items < cap ? items : cap);
   cudaError_t e;
   switch (D) {
