@@ -131,7 +131,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attn_bwd_kernel(Params p) 
   // otherwise pin registers the three products need): warp w owns lanes
   // 32*(w%4).., columns (w/4)*4*NT.., one column per fp32 value of its
   // m16n8 fragments (tile j at columns 4j..4j+3).
-  constexpr uint32_t kTmemCols = NT * 16 <= 32 ? 32 : NT * 16 <= 64 ? 64 : NT * 16 <= 128 ? 128 : NT * 16 <= 256 ? 256 : 512;
+  // The C warps (8..15) park their dkv tile there too, columns 16*NT + ((w-8)/4)*4*NT.
+  constexpr uint32_t kTmemCols = NT * 24 <= 32 ? 32 : NT * 24 <= 64 ? 64 : NT * 24 <= 128 ? 128 : NT * 24 <= 256 ? 256 : 512;
   if (warp == 0) {
     tmem_alloc(sTmem, kTmemCols);
     tmem_relinquish();
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attn_bwd_kernel(Params p) 
   __syncthreads();
   tc_fence_after();
   const uint32_t tdq = *sTmem + ((uint32_t)(32 * hm) << 16) + (uint32_t)((warp >> 2) * 4 * NT);
+  const uint32_t tkv = *sTmem + ((uint32_t)(32 * hm) << 16) + (uint32_t)(16 * NT + (((warp - 8) >> 2) & 1) * 4 * NT);
 
   // cp.async of one tile's kv rows into a stage, indices read from global memory
   auto gather = [&](const int* irow, int b, int t, __nv_bfloat16* stage, int* sidx) {
@@ -210,6 +212,35 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attn_bwd_kernel(Params p) 
       }
     }
 
+    // dkv of the previous tile, parked in tensor memory by the C warps (8..15)
+    // until the next tile's phase 1 runs, so its global reductions overlap that phase
+    float* cdst = nullptr;
+    bool pending = false;
+    const bool codd = t4 & 1;
+    // even lanes (t4 = 0, 2) add row k0, columns 2*t4 .. 2*t4+3; odd lanes add
+    // row k0+8, columns 2*(t4-1) .. +3 (each lane takes its partner's half)
+    auto flush_dkv = [&]() {
+      if (!pending) return;
+      pending = false;
+#pragma unroll 3
+      for (int j2 = 0; j2 < NT; j2 += 2) {
+        float v[8];
+        tmem_ld8_sync(tkv + 4 * j2, v);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float* c = v + 4 * h;
+          const float s0 = codd ? c[0] : c[2], s1 = codd ? c[1] : c[3];
+          const float r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+          if (cdst) {
+            if (codd)
+              red_add_v4(cdst + (j2 + h) * 8, r0, r1, c[2], c[3]);
+            else
+              red_add_v4(cdst + (j2 + h) * 8, c[0], c[1], r0, r1);
+          }
+        }
+      }
+    };
+
 #pragma unroll 1
     for (int t = 0; t < ntiles; ++t) {
       __nv_bfloat16* stage = sKV + (nst == 2 ? (t & 1) : 0) * kKeys * LQ;
@@ -225,58 +256,55 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attn_bwd_kernel(Params p) 
       }
       __syncthreads();  // tile t (and, at t = 0, q / do / delta) visible to all warps
 
-      // ---- 1. S and dO.V^T for heads 16*hm.., keys 8*(warp/4)..
-      {
-        // S over D and dO.V^T over Dv share the kv fragment of each k step;
-        // two accumulator chains each (even / odd k) halve the MMA dependency chain
-        float s[4] = {0.f, 0.f, 0.f, 0.f}, dpv[4] = {0.f, 0.f, 0.f, 0.f};
-        float s2[4] = {0.f, 0.f, 0.f, 0.f}, dpv2[4] = {0.f, 0.f, 0.f, 0.f};
-        const int n0 = 8 * (warp >> 2);
+      if (warp < 8) {
+        // ---- 1. S and dO.V^T for heads 16*hm.., keys 16*(warp/4).. (two n8 tiles);
+        // S over D and dO.V^T over Dv share the kv fragments of each k step
+        const int kq = warp >> 2;
+        float s[2][4], dp[2][4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[0][e] = s[1][e] = dp[0][e] = dp[1][e] = 0.f;
         const uint32_t a_q = smem_u32(sQ + (hm * 16 + (lane & 15)) * LQ + (lane >> 4) * 8);
         const uint32_t a_o = smem_u32(sDO + (hm * 16 + (lane & 15)) * LO + (lane >> 4) * 8);
-        // lanes 16-31 address the next k step (x4 loads: two k steps' fragments)
-        const uint32_t b_kv = smem_u32(stage + (n0 + (lane & 7)) * LQ + ((lane >> 3) & 1) * 8 + (lane >> 4) * 16);
-        const int kv2 = Dv / 32;  // k-step pairs shared by both products
-#pragma unroll 2
-        for (int k2 = 0; k2 < kv2; ++k2) {
+        const uint32_t b_kv = smem_u32(stage + (kq * 16 + (lane & 7) + (lane >> 4) * 8) * LQ + ((lane >> 3) & 1) * 8);
+#pragma unroll 4
+        for (int k = 0; k < Dv / 16; ++k) {
           uint32_t a[4], c[4], bb[4];
-          ldsm_x4(b_kv + k2 * 64, bb);  // k steps 2*k2 (bb[0..1]) and 2*k2+1 (bb[2..3])
-          ldsm_x4(a_q + k2 * 64, a);
-          ldsm_x4(a_o + k2 * 64, c);
-          mma16816(s, a, bb[0], bb[1]);
-          mma16816(dpv, c, bb[0], bb[1]);
-          ldsm_x4(a_q + k2 * 64 + 32, a);
-          ldsm_x4(a_o + k2 * 64 + 32, c);
-          mma16816(s2, a, bb[2], bb[3]);
-          mma16816(dpv2, c, bb[2], bb[3]);
+          ldsm_x4(b_kv + k * 32, bb);
+          ldsm_x4(a_q + k * 32, a);
+          ldsm_x4(a_o + k * 32, c);
+          mma16816(s[0], a, bb[0], bb[1]);
+          mma16816(s[1], a, bb[2], bb[3]);
+          mma16816(dp[0], c, bb[0], bb[1]);
+          mma16816(dp[1], c, bb[2], bb[3]);
         }
 #pragma unroll 4
-        for (int k = 2 * kv2; k < D / 16; ++k) {  // the q.k dims past Dv
-          uint32_t a[4], bb[2];
+        for (int k = Dv / 16; k < D / 16; ++k) {  // the q.k dims past Dv
+          uint32_t a[4], bb[4];
+          ldsm_x4(b_kv + k * 32, bb);
           ldsm_x4(a_q + k * 32, a);
-          ldsm_x2(b_kv + k * 32, bb);
-          mma16816(s, a, bb[0], bb[1]);
+          mma16816(s[0], a, bb[0], bb[1]);
+          mma16816(s[1], a, bb[2], bb[3]);
         }
+        // thread values: heads 16*hm + g (+8); keys 16*kq + 8*nt + 2*t4 (+1)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          s[e] += s2[e];
-          dpv[e] += dpv2[e];
-        }
-        // thread values: heads 16*hm + g (+8); keys n0 + 2*t4 (+1)
-        const int c0 = n0 + 2 * t4;
-        const bool v0 = sid[c0] >= 0, v1 = sid[c0 + 1] >= 0;
+        for (int nt = 0; nt < 2; ++nt) {
+          const int c0 = kq * 16 + nt * 8 + 2 * t4;
+          const bool v0 = sid[c0] >= 0, v1 = sid[c0 + 1] >= 0;
 #pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          const int r = hm * 16 + g + 8 * hr;
-          const bool hv = h0 + r < p.H;
-          const float lse = sLse[r], dl = sDelta[r];
-          const float p0 = (hv && v0) ? expf(s[2 * hr] * p.scale - lse) : 0.f;
-          const float p1 = (hv && v1) ? expf(s[2 * hr + 1] * p.scale - lse) : 0.f;
-          const float d0 = p0 * (dpv[2 * hr] - dl) * p.scale;
-          const float d1 = p1 * (dpv[2 * hr + 1] - dl) * p.scale;
-          *reinterpret_cast<uint32_t*>(sP + r * LP + c0) = pack_bf16x2(p0, p1);
-          *reinterpret_cast<uint32_t*>(sDS + r * LP + c0) = pack_bf16x2(d0, d1);
+          for (int hr = 0; hr < 2; ++hr) {
+            const int r = hm * 16 + g + 8 * hr;
+            const bool hv = h0 + r < p.H;
+            const float lse = sLse[r], dl = sDelta[r];
+            const float p0 = (hv && v0) ? expf(s[nt][2 * hr] * p.scale - lse) : 0.f;
+            const float p1 = (hv && v1) ? expf(s[nt][2 * hr + 1] * p.scale - lse) : 0.f;
+            const float d0 = p0 * (dp[nt][2 * hr] - dl) * p.scale;
+            const float d1 = p1 * (dp[nt][2 * hr + 1] - dl) * p.scale;
+            *reinterpret_cast<uint32_t*>(sP + r * LP + c0) = pack_bf16x2(p0, p1);
+            *reinterpret_cast<uint32_t*>(sDS + r * LP + c0) = pack_bf16x2(d0, d1);
+          }
         }
+      } else {
+        flush_dkv();  // the previous tile's dkv reductions
       }
       __syncthreads();
 
@@ -311,61 +339,44 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attn_bwd_kernel(Params p) 
         }
         tmem_st_wait();
       }
-      // ---- 3. dkv[16 keys x D/8] = dS^T . q + P^T . do, contraction over the 64 heads
-      {
-        const int km = warp & 1, colc = (warp >> 1) * (D / 8);
+      if (warp >= 8) {
+        // ---- 3. dkv[16 keys x D/4] = dS^T . q + P^T . do, contraction over the 64 heads
+        const int c = warp - 8, km = c & 1, colc = (c >> 1) * (D / 4);
         const int arow = (lane >> 4) * 8 + (lane & 7), acol = km * 16 + ((lane >> 3) & 1) * 8;
-        // even lanes (t4 = 0, 2) add row k0, columns 2*t4 .. 2*t4+3; odd lanes add
-        // row k0+8, columns 2*(t4-1) .. +3 (each lane takes its partner's half)
-        const bool odd = t4 & 1;
-        const int v = sid[km * 16 + g + (odd ? 8 : 0)];
-        float* dst = v >= 0 ? p.dkv + ((size_t)b * p.Nkv + v) * D + colc + 2 * (t4 & ~1) : nullptr;
-        // columns in chunks of at most CH n8 tiles (bounds the accumulator registers
-        // that are live beside the dq accumulators)
-        constexpr int CH = NTK > 5 ? (NTK + 1) / 2 : NTK;
+        float cacc[NT][4];
 #pragma unroll
-        for (int j0 = 0; j0 < NTK; j0 += CH) {
-          float acc[CH][4];
+        for (int j = 0; j < NT; ++j) cacc[j][0] = cacc[j][1] = cacc[j][2] = cacc[j][3] = 0.f;
 #pragma unroll
-          for (int j = 0; j < CH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        for (int kh = 0; kh < kHeads / 16; ++kh) {
+          // A = X^T with X [16 heads x 16 keys]: transposed 8x8 blocks
+          uint32_t ads[4], ap[4];
+          ldsm_x4_t(smem_u32(sDS + (kh * 16 + arow) * LP + acol), ads);
+          ldsm_x4_t(smem_u32(sP + (kh * 16 + arow) * LP + acol), ap);
+          const uint32_t bq = smem_u32(sQ + (kh * 16 + (lane & 15)) * LQ + colc + (lane >> 4) * 8);
+          const uint32_t bo = smem_u32(sDO + (kh * 16 + (lane & 15)) * LO + colc + (lane >> 4) * 8);
 #pragma unroll
-          for (int kh = 0; kh < kHeads / 16; ++kh) {
-            // A = X^T with X [16 heads x 16 keys]: transposed 8x8 blocks
-            uint32_t ads[4], ap[4];
-            ldsm_x4_t(smem_u32(sDS + (kh * 16 + arow) * LP + acol), ads);
-            ldsm_x4_t(smem_u32(sP + (kh * 16 + arow) * LP + acol), ap);
-            const uint32_t bq = smem_u32(sQ + (kh * 16 + (lane & 15)) * LQ + colc);
-            const uint32_t bo = smem_u32(sDO + (kh * 16 + (lane & 15)) * LO + colc);
-#pragma unroll
-            for (int j = 0; j < CH; ++j) {
-              const int jj = j0 + j;
-              if (jj < NTK) {
-                uint32_t bb[2];
-                ldsm_x2_t(bq + jj * 16, bb);
-                mma16816(acc[j], ads, bb[0], bb[1]);
-                if (colc + jj * 8 < Dv) {
-                  ldsm_x2_t(bo + jj * 16, bb);
-                  mma16816(acc[j], ap, bb[0], bb[1]);
-                }
-              }
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            const int jj = j0 + j;
-            const float s0 = odd ? acc[j][0] : acc[j][2], s1 = odd ? acc[j][1] : acc[j][3];
-            const float r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
-            if (dst && jj < NTK) {
-              if (odd)
-                red_add_v4(dst + jj * 8, r0, r1, acc[j][2], acc[j][3]);
-              else
-                red_add_v4(dst + jj * 8, acc[j][0], acc[j][1], r0, r1);
+          for (int j = 0; j < NT; j += 2) {
+            uint32_t bb[4];
+            ldsm_x4_t(bq + j * 16, bb);
+            mma16816(cacc[j], ads, bb[0], bb[1]);
+            mma16816(cacc[j + 1], ads, bb[2], bb[3]);
+            if (colc + j * 8 < Dv) {
+              ldsm_x4_t(bo + j * 16, bb);
+              mma16816(cacc[j], ap, bb[0], bb[1]);
+              mma16816(cacc[j + 1], ap, bb[2], bb[3]);
             }
           }
         }
+#pragma unroll
+        for (int j = 0; j < NT; j += 2) tmem_st8(tkv + 4 * j, *reinterpret_cast<float(*)[8]>(&cacc[j][0]));
+        tmem_st_wait();
+        const int v = sid[km * 16 + g + (codd ? 8 : 0)];
+        cdst = v >= 0 ? p.dkv + ((size_t)b * p.Nkv + v) * D + colc + 2 * (t4 & ~1) : nullptr;
+        pending = true;
       }
       __syncthreads();  // stage t and sP / sDS free for the next tile
     }
+    if (warp >= 8) flush_dkv();
     // ---- dq out (heads 16*hm + g (+8); columns col0 + 8j + 2*t4)
     const int col0 = (warp >> 2) * (D / 4);
 #pragma unroll 1
