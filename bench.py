@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--attn-heads", type=int, default=64, help="attention workload: query heads (64; 128 = V4-Pro)")
     ap.add_argument("--attn-k", type=int, default=512, help="attention workload: selected kv rows per query")
     ap.add_argument("--attn-dv", type=int, default=512, help="attention workload: value width (576 = full D)")
+    ap.add_argument("--attn-nkv", type=int, default=16384,
+                    help="attention workload: kv rows (16384 = configs[3]; a power of two above it is a KV cache "
+                         "larger than L2, indices spread over all rows)")
     ap.add_argument("--kv-fp8", action="store_true",
                     help="attention workload: kv stored as FP8 rows (e4m3 NoPE + fp32 block scales + bf16 RoPE)")
     ap.add_argument("--workload", default="indexer", choices=["indexer", "attn", "attn_bwd", "csa"],
@@ -425,18 +428,30 @@ def gen_attn_idx(S, K, n_kv, ratio, device, seed=0, chunk=4096):
     return out
 
 
+def gen_spread_idx(S, K, n_kv, device, seed=0):
+    """K distinct rows per query spread over a power-of-two pool: (a_s + j * c_s) mod n_kv with a random
+    offset a_s and a random odd stride c_s (odd strides are coprime with n_kv, so the K rows are distinct)."""
+    assert n_kv & (n_kv - 1) == 0 and K <= n_kv
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    a0 = torch.randint(0, n_kv, (S, 1), generator=g, device=device)
+    c = torch.randint(0, n_kv // 2, (S, 1), generator=g, device=device) * 2 + 1
+    j = torch.arange(K, device=device).unsqueeze(0)
+    return ((a0 + j * c) % n_kv).to(torch.int32).unsqueeze(0)
+
+
 def run_attn(a):
     """benchmark configs[3]: sparse attention forward, B=1, S=65536, H=64, D=576/512, N_kv=16384, K=512."""
     from streamindex_b200 import _lib
 
-    S, H, D, DV, NKV, K = a.S, a.attn_heads, 576, a.attn_dv, 16384, a.attn_k
+    S, H, D, DV, NKV, K = a.S, a.attn_heads, 576, a.attn_dv, a.attn_nkv, a.attn_k
     device = torch.device("cuda", 0)
     g = torch.Generator(device=device)
     g.manual_seed(0)
     q = torch.randn((1, S, H, D), generator=g, device=device, dtype=torch.bfloat16).mul_(D ** -0.5)
     kv = torch.randn((1, NKV, D), generator=g, device=device, dtype=torch.bfloat16)
     sink = torch.zeros(H, dtype=torch.float32, device=device)
-    idx = gen_attn_idx(S, K, NKV, 4, device)
+    idx = gen_attn_idx(S, K, NKV, 4, device) if NKV == 16384 else gen_spread_idx(S, K, NKV, device)
     o = torch.empty((1, S, H, DV), dtype=torch.bfloat16, device=device)
     lse = torch.empty((1, S, H), dtype=torch.float32, device=device)
     ws = torch.empty(256, dtype=torch.uint8, device=device)
@@ -505,10 +520,13 @@ def run_attn(a):
         "unit": "Mqueries/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; causal uniform indices without replacement)",
-        "config": {"workload": "sparse_attn_fwd%s B=1 S=%d H=%d D_qk=576 D_v=%d N_kv=16384 K=%d" % (
-                       "_fp8kv" if a.kv_fp8 else "", S, H, DV, K),
+        "config": {"workload": "sparse_attn_fwd%s B=1 S=%d H=%d D_qk=576 D_v=%d N_kv=%d K=%d" % (
+                       "_fp8kv" if a.kv_fp8 else "", S, H, DV, NKV, K),
                    "kv_row_bytes": row_bytes,
-                   "valid_slots": V, "l2": "q/o larger than L2; kv (18.9 MB) L2-resident by design"},
+                   "valid_slots": V,
+                   "l2": ("q/o larger than L2; kv (18.9 MB) L2-resident by design" if NKV == 16384 else
+                          "q/o and kv (%.1f GB as stored) larger than L2; indices spread over all rows" % (
+                              NKV * row_bytes / 1e9))},
         "gpu_launches": a.steps,
         "roofline": {"bound": "tensor", "achieved": tf, "peak": tf_peak, "unit": "TFLOP/s", "frac": tf / tf_peak,
                      "peak_source": "of measured (bf16_tflops burst, MEASURED_PEAKS.json)", "traffic": traffic,
