@@ -527,8 +527,12 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
                 }
               }
             }
-            named_bar(1 + hf, 128);
           }
+          // Every warp of the slice has read the counts before any of them
+          // inserts this tile's keys: a count raised by an early insert would
+          // otherwise send only some of the warps into the (barrier-using)
+          // flush.
+          named_bar(1 + hf, 128);
 #pragma unroll
           for (int jj = 0; jj < NQH; ++jj) thr_reg[g][jj] = vthr[g * QG + hf * NQH + jj];
         }
