@@ -491,7 +491,10 @@ __device__ __forceinline__ void indexer_epilogue(const IndexerParams& p, Indexer
           acc[jj] = (sum2(acc2[jj][0]) + sum2(acc2[jj][1])) + (sum2(acc2[jj][2]) + sum2(acc2[jj][3]));
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ms->acc_empty[g]);
+        // The accumulator's TMEM reads completed in tcgen05.wait::ld; a relaxed
+        // arrive keeps the release from waiting on this warp's candidate
+        // stores of the previous group.
+        if (lane == 0) mbar_arrive_relaxed(&ms->acc_empty[g]);
         if (warp == 2 && lane == 0) SI_ITRACE(2, r, t, 4 * g + 2);
 
         if (MODE == kModeScore) {
