@@ -626,7 +626,7 @@ def run_csa(a, world=1, rank=0, local=0):
     headline) and without it."""
     from streamindex_b200.attention import _csa_attn_call
     from streamindex_b200.csa import csa_forward_slice, flash_csa_forward, mean_pool_compress
-    from streamindex_b200.dist import balanced_bounds, gather_to_rank0, legal_pairs
+    from streamindex_b200.dist import balanced_bounds, csa_query_cost_pairs, gather_to_rank0, legal_pairs
     from streamindex_b200.indexer import indexer_topk_slice
 
     B, S, H, D, DV, HI, DI, m, k, nwin = 2, a.S, 64, 576, 512, 64, 128, 4, 512, 128
@@ -637,8 +637,8 @@ def run_csa(a, world=1, rank=0, local=0):
     g.manual_seed(0)
     x_kv = torch.randn((B, S, D), generator=g, device=dev, dtype=torch.bfloat16).mul_(D ** -0.5)
     x_k = torch.randn((B, S, DI), generator=g, device=dev, dtype=torch.bfloat16).mul_(DI ** -0.5)
-    # attention work per query relative to one indexer key: (n_win + k) * H * (D + DV) vs H_I * D_I flops
-    extra = (nwin + k) * H * (D + DV) / (HI * DI)
+    # per-query work beyond the indexer's key pairs (its own fixed cost and the attention), in pair units
+    extra = csa_query_cost_pairs(H, D, DV, HI, DI, nwin, k)
     bounds = balanced_bounds(S, world, T, m, align=128, extra_per_query=extra)
     lo, hi = bounds[rank], bounds[rank + 1]
     gq = torch.Generator(device=dev)

@@ -28,6 +28,20 @@ import torch.distributed as dist
 # rank 0 (the most, and shortest, queries) ~5% more time at 8 GPUs.
 INDEXER_QUERY_COST_PAIRS = 1800.0
 
+# Sparse attention runs at a lower rate than the indexer's dense contraction
+# (config 5 on one B200: indexer 852 TFLOP/s, attention 517 TFLOP/s), so one
+# attention flop costs ~1.65 indexer flops of time.
+ATTN_VS_INDEXER_FLOP_TIME = 1.65
+
+
+def csa_query_cost_pairs(H: int, D: int, Dv: int, HI: int, DI: int, n_win: int, top_k: int) -> float:
+    """Per-query work of a CSA layer that does not grow with s, in indexer
+    key-pair units: the indexer's own per-query cost plus the query's sparse
+    attention over n_win + top_k rows, weighted by the two kernels' measured
+    relative speed."""
+    attn = (n_win + top_k) * H * (D + Dv) / (HI * DI)
+    return INDEXER_QUERY_COST_PAIRS * HI / 64 + ATTN_VS_INDEXER_FLOP_TIME * attn
+
 
 def legal_pairs(S: int, T: int, ratio: Optional[int], lo: int = 0, hi: Optional[int] = None) -> int:
     """Sum over s in [lo, hi) of min(T, (s+1)//ratio) (T per query without a ratio)."""

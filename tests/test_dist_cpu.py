@@ -33,6 +33,23 @@ def test_balanced_bounds_split_work_evenly(N):
     assert max(eq) / min(eq) > 2
 
 
+def test_csa_bounds_weight_the_attention():
+    """CSA slices: the per-query attention cost (weighted by the kernels'
+    measured relative speed) moves queries off the early, attention-heavy
+    ranks; each slice's modelled work is equal."""
+    from streamindex_b200.dist import csa_query_cost_pairs
+
+    S, m = 131072, 4
+    e = csa_query_cost_pairs(64, 576, 512, 64, 128, 128, 512)
+    flops_only = (128 + 512) * 64 * (576 + 512) / (64 * 128)
+    assert e > flops_only
+    b = balanced_bounds(S, 8, S // m, m, align=128, extra_per_query=e)
+    b0 = balanced_bounds(S, 8, S // m, m, align=128, extra_per_query=flops_only)
+    assert b[1] < b0[1]
+    work = [legal_pairs(S, S // m, m, lo, hi) + e * (hi - lo) for lo, hi in zip(b, b[1:])]
+    assert max(work) / min(work) < 1.02  # 128-query alignment
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
