@@ -41,7 +41,8 @@ def test_bwd_golden(golden, name):
 
 
 @pytest.mark.parametrize("B,S,H,D,N,K,dv", [(1, 96, 64, 576, 2048, 512, 512), (2, 40, 24, 256, 300, 70, 256),
-                                            (1, 64, 128, 512, 500, 100, 448)])
+                                            (1, 64, 128, 512, 500, 100, 448), (1, 33, 16, 64, 100, 40, 64),
+                                            (1, 20, 80, 128, 64, 64, 96)])
 def test_bwd_oracle(B, S, H, D, N, K, dv):
     """Config-4 layout (H=64, D=576/512, K=512) at small S, ragged K, H not a
     multiple of 16, masked slots and an all-masked query."""
