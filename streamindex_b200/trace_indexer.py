@@ -73,6 +73,13 @@ def main(S: int = 131072):
     slow = sorted(range(ntiles - 1), key=lambda i: -tile[i])[:12]
     print("  slowest tiles (tile, ns, top-k ns):", [(i, int(tile[i]), int(topk[i])) for i in slow])
     print("  top-k ns over tiles (every 16th):", [int(x) for x in topk[::16]])
+    # the slice's warps meet every 4th tile (flush decision); other tiles only insert
+    for ph in range(4):
+        sel = [i for i in range(ntiles) if i % 4 == ph]
+        tk0 = [(ep[i, 3] - ep[i, 2]).item() for i in sel]
+        tk1 = [(ep[i, 7] - ep[i, 6]).item() for i in sel]
+        print(f"  tiles t % 4 == {ph}: top-k step median g0 {statistics.median(tk0):.0f} ns, "
+              f"g1 {statistics.median(tk1):.0f} ns")
 
 
 if __name__ == "__main__":
